@@ -1,0 +1,296 @@
+// C ABI of the decode engine (include/ek.h): contexts, argument validation,
+// TMA tensor-map encoding and the device status record.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ek.h"
+#include "ek_launch.h"
+
+using ek::KParams;
+
+struct EkContext {
+  int device = 0;
+  ek::DevStatus* status = nullptr;
+  unsigned* counters = nullptr;
+  size_t counters_cap = 0;  // elements
+  __nv_bfloat16* partials = nullptr;
+  size_t partials_cap = 0;  // elements
+  unsigned epoch = 0;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(EK_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map of a row-major [rows, cols] matrix, box 16 rows x 256 cols.
+int encode_matrix(CUtensorMap* m, const void* base, long long rows, long long cols, const char* name) {
+  EncodeTiledFn enc = get_encoder();
+  if (!enc) return fail(EK_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {256, 16};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EK_E_INVALID, "tensor map for %s failed (CUresult %d)", name, (int)r);
+  return EK_SUCCESS;
+}
+
+// bf16 tensor map of a KV cache [L*T, Hkv, D], box D x 1 head x tk tokens.
+int encode_kv(CUtensorMap* m, const void* base, long long rows, int hkv, int d, int tk,
+              const char* name) {
+  EncodeTiledFn enc = get_encoder();
+  if (!enc) return fail(EK_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)hkv, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)d * 2, (cuuint64_t)hkv * d * 2};
+  cuuint32_t box[3] = {(cuuint32_t)d, 1, (cuuint32_t)tk};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EK_E_INVALID, "tensor map for %s failed (CUresult %d)", name, (int)r);
+  return EK_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int grow(EkContext* ctx, size_t counters, size_t partials) {
+  cudaError_t e;
+  if (counters > ctx->counters_cap) {
+    if (ctx->counters) cudaFree(ctx->counters);
+    ctx->counters = nullptr;
+    ctx->counters_cap = 0;
+    if ((e = cudaMalloc(&ctx->counters, counters * sizeof(unsigned))) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(split counters)");
+    if ((e = cudaMemset(ctx->counters, 0, counters * sizeof(unsigned))) != cudaSuccess)
+      return cuda_fail(e, "cudaMemset(split counters)");
+    ctx->counters_cap = counters;
+  }
+  if (partials > ctx->partials_cap) {
+    if (ctx->partials) cudaFree(ctx->partials);
+    ctx->partials = nullptr;
+    ctx->partials_cap = 0;
+    if ((e = cudaMalloc(&ctx->partials, partials * 2)) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(split partials)");
+    ctx->partials_cap = partials;
+  }
+  return EK_SUCCESS;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int ek_abi_version(void) { return EK_ABI_VERSION; }
+
+const char* ek_last_error(void) { return g_err.c_str(); }
+
+int ek_context_create(int device, EkContext** out) {
+  if (!out) return fail(EK_E_INVALID, "out is NULL");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(EK_E_INVALID, "device %d out of range (%d devices)", device, n);
+  DeviceGuard g(device);
+  EkContext* ctx = new EkContext();
+  ctx->device = device;
+  if ((e = cudaMalloc(&ctx->status, sizeof(ek::DevStatus))) != cudaSuccess) {
+    delete ctx;
+    return cuda_fail(e, "cudaMalloc(status)");
+  }
+  if ((e = cudaMemset(ctx->status, 0, sizeof(ek::DevStatus))) != cudaSuccess) {
+    cudaFree(ctx->status);
+    delete ctx;
+    return cuda_fail(e, "cudaMemset(status)");
+  }
+  *out = ctx;
+  return EK_SUCCESS;
+}
+
+void ek_context_destroy(EkContext* ctx) {
+  if (!ctx) return;
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->status) cudaFree(ctx->status);
+  if (ctx->counters) cudaFree(ctx->counters);
+  if (ctx->partials) cudaFree(ctx->partials);
+  delete ctx;
+}
+
+int ek_read_status(EkContext* ctx, EkStatus* out, int clear) {
+  if (!ctx || !out) return fail(EK_E_INVALID, "NULL argument");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  ek::DevStatus s;
+  if ((e = cudaMemcpy(&s, ctx->status, sizeof(s), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpy(status)");
+  static_assert(sizeof(EkStatus) == 8 * sizeof(int32_t), "EkStatus layout");
+  std::memcpy(out, &s, sizeof(EkStatus));
+  if (clear && (e = cudaMemset(ctx->status, 0, sizeof(ek::DevStatus))) != cudaSuccess)
+    return cuda_fail(e, "cudaMemset(status)");
+  return EK_SUCCESS;
+}
+
+int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
+  if (!ctx || !a) return fail(EK_E_INVALID, "NULL context or arguments");
+  const void* required[] = {a->barriers, a->instructions, a->qkv_weights, a->attn_ln_weights,
+                            a->o_weights, a->mlp_ln_weights, a->up_weights, a->gate_weights,
+                            a->down_weights, a->lm_head_norm_weights, a->lm_head_weights,
+                            a->k_cache, a->v_cache, a->rope_cos, a->rope_sin, a->hidden_states,
+                            a->q_post_rope, a->attn_out, a->attn_lse_intermediates,
+                            a->attn_out_intermediates, a->silu_out, a->logits};
+  for (size_t i = 0; i < sizeof(required) / sizeof(required[0]); ++i) {
+    if (!required[i]) return fail(EK_E_INVALID, "pointer argument %zu is NULL", i);
+    if (!aligned16(required[i])) return fail(EK_E_INVALID, "pointer argument %zu is not 16-byte aligned", i);
+  }
+  if (a->timings && !aligned16(a->timings)) return fail(EK_E_INVALID, "timings is not 16-byte aligned");
+
+  const int L = a->num_layers, H = a->hidden, I = a->intermediate, D = a->head_dim;
+  const int Hq = a->num_q_heads, Hkv = a->num_kv_heads, V = a->vocab;
+  if (L < 1 || H < 256 || I < 256 || V < 16 || Hq < 1 || Hkv < 1)
+    return fail(EK_E_INVALID, "bad model dims L=%d H=%d I=%d V=%d Hq=%d Hkv=%d", L, H, I, V, Hq, Hkv);
+  if (D != 64 && D != 128) return fail(EK_E_UNSUPPORTED, "head_dim %d (supported: 64, 128)", D);
+  if (H % 256 || I % 256) return fail(EK_E_INVALID, "hidden and intermediate must be multiples of 256");
+  if (V % 16) return fail(EK_E_INVALID, "vocab %d not a multiple of 16", V);
+  if (Hq % Hkv) return fail(EK_E_INVALID, "num_q_heads %% num_kv_heads != 0");
+  if (Hq * D != H) return fail(EK_E_INVALID, "num_q_heads * head_dim (%d) != hidden (%d)", Hq * D, H);
+  const int gqa = Hq / Hkv;
+  if (gqa > ek::MAX_GQA || ek::CW * gqa * (D + 2) * 4 > ek::ACT_BYTES)
+    return fail(EK_E_UNSUPPORTED, "GQA ratio %d too large for head_dim %d", gqa, D);
+  const int dR = a->down_reduction_size > 0 ? a->down_reduction_size : I;
+  const int oR = a->oproj_reduction_size > 0 ? a->oproj_reduction_size : H;
+  if (dR % 256 || I % dR || I / dR > 255)
+    return fail(EK_E_INVALID, "down_reduction_size %d must be a multiple of 256 dividing %d", dR, I);
+  if (oR % 256 || H % oR || H / oR > 255)
+    return fail(EK_E_INVALID, "oproj_reduction_size %d must be a multiple of 256 dividing %d", oR, H);
+  if (H * 2 > ek::ACT_BYTES || dR * 2 > ek::ACT_BYTES)
+    return fail(EK_E_UNSUPPORTED, "activation vector does not fit in shared memory");
+  if (a->kv_len < 1 || a->rope_rows < 1 || a->max_partials < 1)
+    return fail(EK_E_INVALID, "kv_len, rope_rows and max_partials must be positive");
+  if (a->pos_id < 0 || a->pos_id >= a->kv_len || a->pos_id >= a->rope_rows)
+    return fail(EK_E_INVALID, "pos_id %d outside the KV cache (%d) or rope table (%d)", a->pos_id,
+                a->kv_len, a->rope_rows);
+  if (a->barrier_rows < 6 || a->barrier_cols < Hq + 2 * Hkv)
+    return fail(EK_E_INVALID, "barriers must be at least [L, 6, Hq + 2 Hkv]");
+  if (a->queue_len < 1 || a->num_queues < 1) return fail(EK_E_INVALID, "empty instruction tensor");
+
+  DeviceGuard g(ctx->device);
+  int nsm = 0;
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device);
+  if (a->num_queues > nsm)
+    return fail(EK_E_INVALID, "%d instruction queues but only %d SMs", a->num_queues, nsm);
+
+  const size_t nctr = (size_t)L * 2 * (H / 16);
+  const size_t npart = (size_t)(H / oR + I / dR) * H;
+  int rc = grow(ctx, nctr, npart);
+  if (rc) return rc;
+
+  static KParams p;  // host staging copy; the launch copies it into kernel parameters
+  std::memset(&p, 0, sizeof(p));
+  const int qkv_rows = (Hq + 2 * Hkv) * D;
+  const int tk = ek::HALF_STAGE / (D * 2);
+  if ((rc = encode_matrix(&p.tm_qkv, a->qkv_weights, (long long)L * qkv_rows, H, "qkv_weights"))) return rc;
+  if ((rc = encode_matrix(&p.tm_o, a->o_weights, (long long)L * H, H, "o_weights"))) return rc;
+  if ((rc = encode_matrix(&p.tm_up, a->up_weights, (long long)L * I, H, "up_weights"))) return rc;
+  if ((rc = encode_matrix(&p.tm_gate, a->gate_weights, (long long)L * I, H, "gate_weights"))) return rc;
+  if ((rc = encode_matrix(&p.tm_down, a->down_weights, (long long)L * H, I, "down_weights"))) return rc;
+  if ((rc = encode_matrix(&p.tm_lm, a->lm_head_weights, V, H, "lm_head_weights"))) return rc;
+  if ((rc = encode_kv(&p.tm_k, a->k_cache, (long long)L * a->kv_len, Hkv, D, tk, "k_cache"))) return rc;
+  if ((rc = encode_kv(&p.tm_v, a->v_cache, (long long)L * a->kv_len, Hkv, D, tk, "v_cache"))) return rc;
+
+  p.barriers = a->barriers;
+  p.instructions = a->instructions;
+  p.timings = a->timings;
+  p.attn_ln = static_cast<const __nv_bfloat16*>(a->attn_ln_weights);
+  p.mlp_ln = static_cast<const __nv_bfloat16*>(a->mlp_ln_weights);
+  p.lm_norm = static_cast<const __nv_bfloat16*>(a->lm_head_norm_weights);
+  p.k_cache = static_cast<__nv_bfloat16*>(a->k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(a->v_cache);
+  p.rope_cos = a->rope_cos;
+  p.rope_sin = a->rope_sin;
+  p.hidden = static_cast<__nv_bfloat16*>(a->hidden_states);
+  p.q = static_cast<__nv_bfloat16*>(a->q_post_rope);
+  p.attn_out = static_cast<__nv_bfloat16*>(a->attn_out);
+  p.lse = a->attn_lse_intermediates;
+  p.attn_o = a->attn_out_intermediates;
+  p.silu = static_cast<__nv_bfloat16*>(a->silu_out);
+  p.logits = static_cast<__nv_bfloat16*>(a->logits);
+  p.status = ctx->status;
+  p.split_counters = ctx->counters;
+  p.split_partials = ctx->partials;
+  p.L = L; p.H = H; p.I = I; p.D = D; p.Hq = Hq; p.Hkv = Hkv; p.V = V;
+  p.T = a->kv_len; p.rope_rows = a->rope_rows; p.maxP = a->max_partials;
+  p.brow = a->barrier_rows; p.bcol = a->barrier_cols;
+  p.nq = a->num_queues; p.Q = a->queue_len;
+  p.qkv_rows = qkv_rows; p.gqa = gqa; p.tk = tk;
+  p.pos = a->pos_id; p.skip_red = a->skip_attn_reduction ? 1 : 0;
+  p.scale = a->attn_scale; p.eps = a->rms_norm_eps;
+  p.down_R = dR; p.o_R = oR; p.down_splits = I / dR; p.o_splits = H / oR;
+  p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
+  p.record = a->record_timings && a->timings ? 1 : 0;
+  p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
+  if (++ctx->epoch == 0) ctx->epoch = 1;
+  p.epoch = ctx->epoch;
+
+  cudaError_t e = ek::launch_decode(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+  return EK_SUCCESS;
+}
+
+}  // extern "C"

@@ -1,0 +1,716 @@
+// Llama batch-1 decode megakernel: loader and consumer roles, the opcode
+// bodies, and the host-side launcher (ek_launch_llama).
+//
+// Opcode semantics follow megakernels/demos/latency/python_vm.py of
+// epic-kernel (cited per op); see ek_kernel.cuh for the overall design.
+#include <cuda_runtime.h>
+
+#include "ek_kernel.cuh"
+#include "ek_launch.h"
+
+namespace ek {
+
+// ------------------------------------------------------------------ consumer helpers
+struct Consumer {
+  const KParams& p;
+  Ring ring;
+  uint8_t* act;     // ACT_BYTES: bf16 activation vector or attention merge area
+  float* red;       // CW floats of reduction scratch
+  int* flag;        // one int broadcast between consumer threads
+  int tid, warp, lane;
+  int qidx, iidx;   // queue and instruction index (error reports, timings)
+  bool broken;      // the ring stalled: leave the kernel
+
+  __device__ Consumer(const KParams& p_) : p(p_) {}
+
+  __device__ __forceinline__ void sync() { named_sync<NC>(); }
+
+  // Wait for stage data; every consumer warp calls this for every stage.
+  __device__ __forceinline__ const uint8_t* acquire() {
+    if (!ring_wait(&ring.full[ring.slot], ring.phase, 4 * p.timeout_ns + 2000000000ll)) {
+      if (lane == 0) record_error(p, 4, iidx, -1, -1, ring.slot, (int)ring.phase, warp);
+      broken = true;
+    }
+    return ring.stages + (size_t)ring.slot * STAGE_BYTES;
+  }
+
+  __device__ __forceinline__ void release() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.empty[ring.slot]);
+    ring_advance(ring);
+  }
+
+  __device__ void drain(int ns) {
+    for (int k = 0; k < ns && !broken; ++k) {
+      acquire();
+      release();
+    }
+  }
+
+  // Thread 0 spins until every counter in `addrs` reaches its target, bounded
+  // by p.timeout_ns. Returns (to all consumer threads) whether to run the op.
+  __device__ bool wait_counters(int n, int* const* addrs, const int* targets, int opcode, int layer) {
+    if (tid == 0) {
+      int ok = 1;
+      for (int j = 0; j < n && ok; ++j) {
+        int v = ld_acquire(addrs[j]);
+        if (v >= targets[j]) continue;
+        const uint64_t t0 = globaltimer();
+        for (uint32_t it = 0;; ++it) {
+          v = ld_acquire(addrs[j]);
+          if (v >= targets[j]) break;
+          if ((it & 15u) == 15u) {
+            if (aborted(p)) { ok = 0; break; }
+            if ((long long)(globaltimer() - t0) > p.timeout_ns) {
+              record_error(p, 1, iidx, opcode, layer, v, targets[j],
+                           (int)(addrs[j] - p.barriers));
+              ok = 0;
+              break;
+            }
+          }
+          __nanosleep(32);
+        }
+      }
+      if (ok && aborted(p)) ok = 0;
+      *flag = ok;
+    }
+    sync();
+    const bool ok = *flag != 0;
+    sync();
+    return ok;
+  }
+
+  __device__ __forceinline__ int* bar(int layer, int row, int col) const {
+    return p.barriers + ((size_t)layer * p.brow + row) * p.bcol + col;
+  }
+
+  __device__ __forceinline__ void stamp(int slot) {
+    if (p.record && tid == 0 && p.timings)
+      p.timings[((size_t)qidx * p.Q + iidx) * 128 + slot] = (int)(globaltimer() & 0x7fffffff);
+  }
+
+  // xs[i] = bf16(w[i] * bf16(x[i] * rsqrt(mean(x^2) + eps))) for the n-vector at
+  // `x` (python_vm.py:50-56). Leaves xs in `act`.
+  __device__ void rmsnorm_to_act(const __nv_bfloat16* x, const __nv_bfloat16* wt, int n) {
+    uint4* xs4 = reinterpret_cast<uint4*>(act);
+    const uint4* x4 = reinterpret_cast<const uint4*>(x);
+    const uint4* w4 = reinterpret_cast<const uint4*>(wt);
+    float ss = 0.f;
+    for (int c = tid; c < n / 8; c += NC) {
+      uint4 v = __ldcg(x4 + c);
+      xs4[c] = v;
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = bf_lo(u[k]), b = bf_hi(u[k]);
+        ss = fmaf(a, a, ss);
+        ss = fmaf(b, b, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    sync();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < CW; ++k) tot += red[k];
+    const float r = 1.0f / sqrtf(tot / (float)n + p.eps);
+    for (int c = tid; c < n / 8; c += NC) {
+      const uint4 v = xs4[c];
+      const uint4 g = __ldg(w4 + c);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float lo = bf_lo(gw[k]) * bf16r(bf_lo(u[k]) * r);
+        const float hi = bf_hi(gw[k]) * bf16r(bf_hi(u[k]) * r);
+        o[k] = pack_bf16x2(lo, hi);
+      }
+      xs4[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    sync();
+  }
+
+  // Copy n bf16 (n % 8 == 0) from global to act (values other SMs wrote).
+  __device__ void copy_to_act(const __nv_bfloat16* x, int n) {
+    uint4* xs4 = reinterpret_cast<uint4*>(act);
+    const uint4* x4 = reinterpret_cast<const uint4*>(x);
+    for (int c = tid; c < n / 8; c += NC) xs4[c] = __ldcg(x4 + c);
+    sync();
+  }
+
+  // Accumulate the stage's 16 x (256 or 512) tile against xs[x0 ...] into the
+  // two rows (2 warp, 2 warp + 1) this warp owns.
+  __device__ __forceinline__ void mac_stage(const uint8_t* st, int x0, bool two, float& a0, float& a1) {
+    const uint4* xs4 = reinterpret_cast<const uint4*>(act);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !two) break;
+      const uint4 xv = xs4[(x0 + h * 256) / 8 + lane];
+      const uint8_t* base = st + h * HALF_STAGE + lane * 16;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(base + (2 * warp) * 512);
+      const uint4 w1 = *reinterpret_cast<const uint4*>(base + (2 * warp + 1) * 512);
+      const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+      const uint32_t u0[4] = {w0.x, w0.y, w0.z, w0.w};
+      const uint32_t u1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float xl = bf_lo(xu[k]), xh = bf_hi(xu[k]);
+        a0 = fmaf(bf_lo(u0[k]), xl, a0);
+        a0 = fmaf(bf_hi(u0[k]), xh, a0);
+        a1 = fmaf(bf_lo(u1[k]), xl, a1);
+        a1 = fmaf(bf_hi(u1[k]), xh, a1);
+      }
+    }
+  }
+
+  // One 16-row block reduced over K columns (xs holds those K values starting
+  // at act[0]); returns the full row sums in every lane.
+  __device__ __forceinline__ void gemv_block(int K, float& r0, float& r1) {
+    const int spb = stages_per_row_block(K);
+    float a0 = 0.f, a1 = 0.f;
+    for (int s = 0; s < spb; ++s) {
+      const uint8_t* st = acquire();
+      if (broken) return;
+      mac_stage(st, s * GEMV_STAGE_COLS, s * GEMV_STAGE_COLS + 256 < K, a0, a1);
+      release();
+    }
+    r0 = warp_sum(a0);
+    r1 = warp_sum(a1);
+  }
+
+  // ---------------------------------------------------------------- opcodes
+  // LayerNorm_QKV_MatVecRopeAppend (python_vm.py:182-262).
+  __device__ void op_qkv(const Ins& ins, const Plan& pl) {
+    const int l = ins.w[1], b0 = ins.w[2], b1 = ins.w[3];
+    if (l > 0) {
+      int* a = bar(l - 1, OP_DOWN - 1, 0);
+      const int t = p.down_splits * (p.H / 16);
+      if (!wait_counters(1, &a, &t, OP_QKV, l)) { drain(pl.ns); return; }
+    } else if (aborted(p)) {
+      drain(pl.ns);
+      return;
+    }
+    stamp(1);
+    rmsnorm_to_act(p.hidden, p.attn_ln + (size_t)l * p.H, p.H);
+    const int qdim = p.Hq * p.D, kdim = p.Hkv * p.D;
+    for (int b = b0; b < b1; ++b) {
+      float r0, r1;
+      gemv_block(p.H, r0, r1);
+      if (broken) return;
+      if (lane == 0) {
+        const int row = b * 16 + 2 * warp;  // even: rows (row, row + 1) form a rotary pair
+        float v0 = bf16r(r0), v1 = bf16r(r1);
+        if (row < qdim + kdim) {
+          // interleaved RoPE (llama.py:136-174) in fp32, rounded to bf16 on store
+          const int seg = row % p.D;
+          const float* cs = p.rope_cos + (size_t)p.pos * p.D + seg;
+          const float* sn = p.rope_sin + (size_t)p.pos * p.D + seg;
+          const float o0 = __fadd_rn(__fmul_rn(v0, cs[0]), __fmul_rn(-v1, sn[0]));
+          const float o1 = __fadd_rn(__fmul_rn(v1, cs[1]), __fmul_rn(v0, sn[1]));
+          v0 = o0;
+          v1 = o1;
+        }
+        const uint32_t packed = pack_bf16x2(v0, v1);
+        __nv_bfloat16* dst;
+        if (row < qdim) {
+          dst = p.q + row;
+        } else if (row < qdim + kdim) {
+          dst = p.k_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim);
+        } else {
+          dst = p.v_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim - kdim);
+        }
+        *reinterpret_cast<uint32_t*>(dst) = packed;
+      }
+    }
+    sync();
+    if (tid == 0) {
+      __threadfence();
+      const int bph = p.D / 16;
+      int b = b0;
+      while (b < b1) {
+        const int head = b / bph;
+        int cnt = 0;
+        while (b < b1 && b / bph == head) { ++cnt; ++b; }
+        red_release_add(bar(l, OP_QKV - 1, head), cnt);
+      }
+    }
+  }
+
+  // Per-lane dims of one KV row: D / 32 consecutive elements.
+  template <int D>
+  __device__ __forceinline__ void load_row(const __nv_bfloat16* src, float* out, bool global) {
+    constexpr int DPL = D / 32;
+    if constexpr (DPL == 2) {
+      const uint32_t u = global ? __ldcg(reinterpret_cast<const unsigned*>(src) + lane)
+                                : reinterpret_cast<const uint32_t*>(src)[lane];
+      out[0] = bf_lo(u);
+      out[1] = bf_hi(u);
+    } else {
+      const uint2 u = global ? __ldcg(reinterpret_cast<const uint2*>(src) + lane)
+                             : reinterpret_cast<const uint2*>(src)[lane];
+      out[0] = bf_lo(u.x);
+      out[1] = bf_hi(u.x);
+      out[2] = bf_lo(u.y);
+      out[3] = bf_hi(u.y);
+    }
+  }
+
+  template <int D>
+  struct AttnState {
+    float q[MAX_GQA][D / 32];
+    float m[MAX_GQA], l[MAX_GQA];
+    float acc[MAX_GQA][D / 32];
+  };
+
+  template <int D>
+  __device__ __forceinline__ void attend(AttnState<D>& s, const float* k, const float* v, int gqa) {
+    constexpr int DPL = D / 32;
+#pragma unroll
+    for (int h = 0; h < MAX_GQA; ++h) {
+      if (h >= gqa) break;
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) d = fmaf(s.q[h][e], k[e], d);
+      const float sc = warp_sum(d) * p.scale;
+      const float mn = fmaxf(s.m[h], sc);
+      const float corr = expf(s.m[h] - mn);
+      const float pe = expf(sc - mn);
+      s.l[h] = s.l[h] * corr + pe;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) s.acc[h][e] = fmaf(pe, v[e], s.acc[h][e] * corr);
+      s.m[h] = mn;
+    }
+  }
+
+  // PartialAttention (python_vm.py:291-357): softmax(q K^T * scale) V over the
+  // partial's token slice for the query heads of one KV head; LSE is
+  // log2(sum(exp(scores))).
+  template <int D>
+  __device__ void op_partial(const Ins& ins, const Plan& pl) {
+    constexpr int DPL = D / 32;
+    const int l = ins.w[1], kvh = ins.w[2], P = ins.w[3], part = ins.w[4];
+    const int gqa = p.gqa, hs = kvh * gqa, bph = D / 16;
+    {
+      int* a[MAX_GQA + 2];
+      int t[MAX_GQA + 2];
+      for (int h = 0; h < gqa; ++h) { a[h] = bar(l, OP_QKV - 1, hs + h); t[h] = bph; }
+      a[gqa] = bar(l, OP_QKV - 1, p.Hq + kvh);
+      a[gqa + 1] = bar(l, OP_QKV - 1, p.Hq + p.Hkv + kvh);
+      t[gqa] = t[gqa + 1] = bph;
+      if (!wait_counters(gqa + 2, a, t, OP_PARTIAL, l)) { drain(pl.ns); return; }
+    }
+    stamp(1);
+    const TokenRange tr = partial_tokens(p, P, part);
+    AttnState<D> s;
+#pragma unroll
+    for (int h = 0; h < MAX_GQA; ++h) {
+      s.m[h] = -INFINITY;
+      s.l[h] = 0.f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) s.acc[h][e] = 0.f;
+      if (h < gqa) load_row<D>(p.q + (size_t)(hs + h) * D, s.q[h], true);
+    }
+    const int kvrow = p.Hkv * D;
+    for (int k = 0; k < pl.ns; ++k) {
+      const uint8_t* st = acquire();
+      if (broken) return;
+      const int t0 = tr.t_begin + k * p.tk;
+      for (int j = warp; j < p.tk; j += CW) {
+        if (t0 + j >= tr.t_load_end) break;
+        float kv[DPL], vv[DPL];
+        load_row<D>(reinterpret_cast<const __nv_bfloat16*>(st + j * D * 2), kv, false);
+        load_row<D>(reinterpret_cast<const __nv_bfloat16*>(st + HALF_STAGE + j * D * 2), vv, false);
+        attend<D>(s, kv, vv, gqa);
+      }
+      release();
+    }
+    // the token appended by this step's QKV instructions is read from global
+    if (warp == 0 && p.pos >= tr.t_begin && p.pos < tr.t_end) {
+      float kv[DPL], vv[DPL];
+      const size_t off = ((size_t)l * p.T + p.pos) * kvrow + (size_t)kvh * D;
+      load_row<D>(p.k_cache + off, kv, true);
+      load_row<D>(p.v_cache + off, vv, true);
+      attend<D>(s, kv, vv, gqa);
+    }
+    // merge the per-warp online-softmax states
+    float* mm = reinterpret_cast<float*>(act);          // [CW][gqa]
+    float* ll = mm + CW * MAX_GQA;                      // [CW][gqa]
+    float* aa = ll + CW * MAX_GQA;                      // [CW][gqa][D]
+#pragma unroll
+    for (int h = 0; h < MAX_GQA; ++h) {
+      if (h >= gqa) break;
+      if (lane == 0) {
+        mm[warp * gqa + h] = s.m[h];
+        ll[warp * gqa + h] = s.l[h];
+      }
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) aa[(warp * gqa + h) * D + lane * DPL + e] = s.acc[h][e];
+    }
+    sync();
+    for (int idx = tid; idx < gqa * D; idx += NC) {
+      const int h = idx / D, d = idx % D;
+      float M = -INFINITY;
+      for (int w = 0; w < CW; ++w) M = fmaxf(M, mm[w * gqa + h]);
+      float Ls = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int w = 0; w < CW; ++w) {
+          const float f = expf(mm[w * gqa + h] - M);
+          Ls = fmaf(ll[w * gqa + h], f, Ls);
+          O = fmaf(aa[(w * gqa + h) * D + d], f, O);
+        }
+      }
+      float out, lse;
+      if (Ls > 0.f) {
+        out = O / Ls;
+        lse = log2f(Ls) + M * 1.4426950408889634f;
+      } else {
+        out = 0.f;
+        lse = -INFINITY;
+      }
+      const int head = hs + h;
+      if (p.skip_red) {
+        p.attn_out[(size_t)head * D + d] = __float2bfloat16_rn(out);
+      } else {
+        p.attn_o[((size_t)head * p.maxP + part) * D + d] = out;
+        if (d == 0) p.lse[(size_t)head * p.maxP + part] = lse;
+      }
+    }
+    sync();
+    if (tid == 0) {
+      __threadfence();
+      if (p.skip_red) {
+        red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
+      } else {
+        for (int h = 0; h < gqa; ++h) red_release_add(bar(l, OP_PARTIAL - 1, hs + h), 1);
+      }
+    }
+  }
+
+  // AttentionReduction (python_vm.py:360-401): exp2-weighted merge of partials.
+  __device__ void op_reduction(const Ins& ins) {
+    const int l = ins.w[1], hs = ins.w[2], P = ins.w[3], terminal = ins.w[4], n = ins.w[5];
+    const int out_slot = ins.w[6 + n];
+    {
+      int* a = bar(l, OP_PARTIAL - 1, hs);
+      if (!wait_counters(1, &a, &P, OP_REDUCTION, l)) return;
+    }
+    stamp(1);
+    const int D = p.D, gqa = p.gqa;
+    // compute first, write after a barrier: the output slot may be an input
+    float res[4], newlse[4];
+    int cnt = 0;
+    for (int idx = tid; idx < gqa * D; idx += NC, ++cnt) {
+      const int h = idx / D, d = idx % D;
+      const size_t row = (size_t)(hs + h) * p.maxP;
+      float M = -INFINITY;
+      for (int j = 0; j < n; ++j) M = fmaxf(M, __ldcg(p.lse + row + ins.w[6 + j]));
+      float den = 0.f, num = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const int slot = ins.w[6 + j];
+        const float f = exp2f(__ldcg(p.lse + row + slot) - M);
+        den += f;
+        num = fmaf(__ldcg(p.attn_o + (row + slot) * D + d), f, num);
+      }
+      res[cnt] = num / den;
+      newlse[cnt] = logf(den);
+    }
+    sync();
+    cnt = 0;
+    for (int idx = tid; idx < gqa * D; idx += NC, ++cnt) {
+      const int h = idx / D, d = idx % D;
+      if (terminal) {
+        p.attn_out[(size_t)(hs + h) * D + d] = __float2bfloat16_rn(res[cnt]);
+      } else {
+        const size_t row = (size_t)(hs + h) * p.maxP + out_slot;
+        p.attn_o[row * D + d] = res[cnt];
+        if (d == 0) p.lse[row] = newlse[cnt];
+      }
+    }
+    sync();
+    if (tid == 0) {
+      __threadfence();
+      red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
+    }
+  }
+
+  // Epoch-tagged arrival counter: returns the arrival number (1-based) of this
+  // call in the current launch. Counters left by an aborted launch are stale
+  // (different epoch) and restart at 1.
+  __device__ __forceinline__ unsigned arrive_split(unsigned* ctr) {
+    const unsigned tag = (p.epoch & 0xffffffu) << 8;
+    unsigned old = *reinterpret_cast<volatile unsigned*>(ctr);
+    while (true) {
+      const unsigned nv = ((old & ~0xffu) == tag) ? old + 1 : (tag | 1u);
+      const unsigned prev = atomicCAS(ctr, old, nv);
+      if (prev == old) return nv & 0xffu;
+      old = prev;
+    }
+  }
+
+  // hidden[rows] += W[rows, split cols] . x  for O_ProjResidual / DownProjResidual
+  // (python_vm.py:59-80, 101-139). With several column splits, each split
+  // stores its bf16 partial; the last split to arrive for a 16-row block adds
+  // the partials to hidden in split order, as the interpreter does.
+  __device__ void op_matvec_add(const Ins& ins, const Plan& pl) {
+    const bool o = pl.op == OP_OPROJ;
+    const int l = ins.w[1], b0 = ins.w[2], b1 = ins.w[3], split = ins.w[4];
+    const int R = o ? p.o_R : p.down_R;
+    const int splits = o ? p.o_splits : p.down_splits;
+    {
+      int* a = o ? bar(l, OP_REDUCTION - 1, 0) : bar(l, OP_UPGATE - 1, 0);
+      const int t = o ? p.Hq : p.I / 16;
+      if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
+    }
+    stamp(1);
+    copy_to_act((o ? p.attn_out : p.silu) + (size_t)split * R, R);
+    // partial sums: [o_splits][H] for O_ProjResidual, then [down_splits][H]
+    __nv_bfloat16* partials = p.split_partials + (size_t)(o ? 0 : p.o_splits) * p.H;
+    for (int b = b0; b < b1; ++b) {
+      float r0, r1;
+      gemv_block(R, r0, r1);
+      if (broken) return;
+      if (lane == 0) {
+        const int row = b * 16 + 2 * warp;
+        const float v0 = bf16r(r0), v1 = bf16r(r1);
+        if (splits == 1) {
+          const uint32_t h = __ldcg(reinterpret_cast<const unsigned*>(p.hidden + row));
+          *reinterpret_cast<uint32_t*>(p.hidden + row) = pack_bf16x2(bf_lo(h) + v0, bf_hi(h) + v1);
+        } else {
+          *reinterpret_cast<uint32_t*>(partials + (size_t)split * p.H + row) = pack_bf16x2(v0, v1);
+        }
+      }
+    }
+    sync();
+    int* done = bar(l, pl.op - 1, 0);
+    if (splits == 1) {
+      if (tid == 0) {
+        __threadfence();
+        red_release_add(done, b1 - b0);
+      }
+      return;
+    }
+    unsigned* ctrs = p.split_counters + ((size_t)l * 2 + (o ? 0 : 1)) * (p.H / 16);
+    for (int b = b0 + warp; b < b1; b += CW) {
+      unsigned arrival = 0;
+      if (lane == 0) {
+        __threadfence();
+        arrival = arrive_split(ctrs + b);
+      }
+      arrival = __shfl_sync(0xffffffffu, arrival, 0);
+      if (arrival == (unsigned)splits) {
+        __threadfence();
+        if (lane < 16) {
+          const int row = b * 16 + lane;
+          float h = ldcg_bf16(p.hidden + row);
+          for (int c = 0; c < splits; ++c) h = bf16r(h + ldcg_bf16(partials + (size_t)c * p.H + row));
+          p.hidden[row] = __float2bfloat16_rn(h);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          red_release_add(done, splits);
+        }
+      }
+    }
+  }
+
+  // LayerNormDoubleMatVecSiLU (python_vm.py:142-179): silu(gate) * up per block.
+  __device__ void op_upgate(const Ins& ins, const Plan& pl) {
+    const int l = ins.w[1], n = ins.w[2];
+    {
+      int* a = bar(l, OP_OPROJ - 1, 0);
+      const int t = p.H / 16;
+      if (!wait_counters(1, &a, &t, OP_UPGATE, l)) { drain(pl.ns); return; }
+    }
+    stamp(1);
+    rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H);
+    for (int j = 0; j < n; ++j) {
+      float u0, u1, g0, g1;
+      gemv_block(p.H, u0, u1);
+      if (broken) return;
+      gemv_block(p.H, g0, g1);
+      if (broken) return;
+      if (lane == 0) {
+        const int row = ins.w[3 + j] * 16 + 2 * warp;
+        const float gb0 = bf16r(g0), gb1 = bf16r(g1);
+        const float s0 = bf16r(gb0 / (1.0f + expf(-gb0)));
+        const float s1 = bf16r(gb1 / (1.0f + expf(-gb1)));
+        *reinterpret_cast<uint32_t*>(p.silu + row) = pack_bf16x2(s0 * bf16r(u0), s1 * bf16r(u1));
+      }
+    }
+    sync();
+    if (tid == 0) {
+      __threadfence();
+      red_release_add(bar(l, OP_UPGATE - 1, 0), n);
+    }
+  }
+
+  // RMS_LM_Head (python_vm.py:265-288): logits rows of the final RMSNorm'd hidden.
+  __device__ void op_lm_head(const Ins& ins, const Plan& pl) {
+    const int b0 = ins.w[1], b1 = ins.w[2];
+    {
+      int* a = bar(p.L - 1, OP_DOWN - 1, 0);
+      const int t = p.down_splits * (p.H / 16);
+      if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
+    }
+    stamp(1);
+    rmsnorm_to_act(p.hidden, p.lm_norm, p.H);
+    for (int b = b0; b < b1; ++b) {
+      float r0, r1;
+      gemv_block(p.H, r0, r1);
+      if (broken) return;
+      if (lane == 0)
+        *reinterpret_cast<uint32_t*>(p.logits + b * 16 + 2 * warp) = pack_bf16x2(r0, r1);
+    }
+  }
+};
+
+// ------------------------------------------------------------------ loader
+__device__ void run_loader(const KParams& p, Ring ring) {
+  const int q = blockIdx.x;
+  Ins ins, pins;
+  Plan pl, ppl;
+  // prefetch cursor (L2 lookahead beyond the ring)
+  int pi = 0, pk = 0;
+  bool p_valid = false;
+  long long g_load = 0, g_pf = 0;
+  const bool pf_on = p.pf_stages > 0;
+
+  for (int i = 0; i < p.Q; ++i) {
+    fetch_ins(p, q, i, ins);
+    pl = make_plan(p, ins);
+    for (int k = 0; k < pl.ns; ++k) {
+      if (pf_on) {
+        while (g_pf < g_load + p.pf_stages) {
+          if (!p_valid) {
+            if (pi >= p.Q) break;
+            fetch_ins(p, q, pi, pins);
+            ppl = make_plan(p, pins);
+            pk = 0;
+            p_valid = true;
+          }
+          if (pk >= ppl.ns) {
+            ++pi;
+            p_valid = false;
+            continue;
+          }
+          if (g_pf >= g_load) do_stage<true>(p, pins, ppl, pk, nullptr, nullptr);
+          ++pk;
+          ++g_pf;
+        }
+      }
+      if (!ring_wait(&ring.empty[ring.slot], ring.phase ^ 1u, 4 * p.timeout_ns + 2000000000ll)) {
+        record_error(p, 4, i, pl.op, pl.layer, ring.slot, (int)ring.phase, -1);
+        return;
+      }
+      do_stage<false>(p, ins, pl, k, ring.stages + (size_t)ring.slot * STAGE_BYTES,
+                      &ring.full[ring.slot]);
+      ring_advance(ring);
+      ++g_load;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ kernel
+template <int D>
+__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ KParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* stages = smem;
+  uint8_t* act = smem + NUM_STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(act + ACT_BYTES);
+  uint64_t* empty = full + NUM_STAGES;
+  float* red = reinterpret_cast<float*>(empty + NUM_STAGES);
+  int* flag = reinterpret_cast<int*>(red + CW);
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  if (tid == 0) {
+    for (int s = 0; s < NUM_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CW);
+    }
+    fence_mbar_init();
+  }
+  if (tid == NC) {
+    prefetch_tensormap(&p.tm_qkv);
+    prefetch_tensormap(&p.tm_o);
+    prefetch_tensormap(&p.tm_up);
+    prefetch_tensormap(&p.tm_gate);
+    prefetch_tensormap(&p.tm_down);
+    prefetch_tensormap(&p.tm_lm);
+    prefetch_tensormap(&p.tm_k);
+    prefetch_tensormap(&p.tm_v);
+  }
+  __syncthreads();
+
+  Ring ring{stages, full, empty, 0, 0u};
+  if (warp == CW) {
+    if (lane == 0) run_loader(p, ring);
+    return;
+  }
+
+  Consumer c(p);
+  c.ring = ring;
+  c.act = act;
+  c.red = red;
+  c.flag = flag;
+  c.tid = tid;
+  c.warp = warp;
+  c.lane = lane;
+  c.qidx = blockIdx.x;
+  c.broken = false;
+
+  Ins ins;
+  for (int i = 0; i < p.Q && !c.broken; ++i) {
+    c.iidx = i;
+    fetch_ins(p, blockIdx.x, i, ins);
+    const Plan pl = make_plan(p, ins);
+    c.stamp(0);
+    if (pl.bad_word >= 0) {
+      if (tid == 0)
+        record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > OP_LM_HEAD) ? 2 : 3, i, pl.op,
+                     pl.layer, 0, pl.bad_word, ins.w[pl.bad_word]);
+      continue;  // no stages were planned for it
+    }
+    switch (pl.op) {
+      case OP_NOOP: break;
+      case OP_QKV: c.op_qkv(ins, pl); break;
+      case OP_PARTIAL: c.op_partial<D>(ins, pl); break;
+      case OP_REDUCTION: c.op_reduction(ins); break;
+      case OP_OPROJ:
+      case OP_DOWN: c.op_matvec_add(ins, pl); break;
+      case OP_UPGATE: c.op_upgate(ins, pl); break;
+      case OP_LM_HEAD: c.op_lm_head(ins, pl); break;
+      default: break;
+    }
+    c.stamp(2);
+    c.sync();  // act / red / flag are reused by the next instruction
+  }
+}
+
+// ------------------------------------------------------------------ host launch
+cudaError_t launch_decode(const KParams& p, cudaStream_t stream) {
+  static bool attr_done[2] = {false, false};
+  const void* fn = p.D == 64 ? reinterpret_cast<const void*>(&decode_kernel<64>)
+                             : reinterpret_cast<const void*>(&decode_kernel<128>);
+  const int which = p.D == 64 ? 0 : 1;
+  if (!attr_done[which]) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done[which] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.nq);
+  cfg.blockDim = dim3(NTHREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (p.D == 64) return cudaLaunchKernelEx(&cfg, decode_kernel<64>, p);
+  return cudaLaunchKernelEx(&cfg, decode_kernel<128>, p);
+}
+
+}  // namespace ek

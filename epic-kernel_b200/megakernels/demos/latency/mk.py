@@ -1,0 +1,70 @@
+"""Calling the Llama megakernel with a `Globals` bundle
+(`megakernels/demos/latency/mk.py` of epic-kernel, :11-68): the 5-D KV caches
+are viewed as 4-D `[(L * B), T, Hkv, D]` and the tensors passed in the
+module's positional order on the current stream."""
+
+from pathlib import Path
+
+import torch
+
+from megakernels.demos.latency.instructions import Globals
+from megakernels.mk import MK_Interpreter, _add_to_path
+
+
+def interpret_with_mk(globs: Globals, mk_func, **options):
+    k4 = globs.k_cache.flatten(0, 1)
+    v4 = globs.v_cache.flatten(0, 1)
+    mk_func(
+        globs.barriers,
+        globs.instructions,
+        globs.timings,
+        globs.qkv_proj_weights,
+        globs.attn_ln_weights,
+        globs.o_proj_weights,
+        globs.mlp_ln_weights,
+        globs.up_proj_weights,
+        globs.gate_proj_weights,
+        globs.down_proj_weights,
+        globs.lm_head_norm_weights.data,
+        globs.lm_head_weights.data,
+        k4,
+        v4,
+        globs.rope_cos,
+        globs.rope_sin,
+        globs.hidden_states,
+        globs.post_ln_rope_q,
+        globs.attn_out,
+        globs.attn_lse_intermediates,
+        globs.attn_out_intermediates,
+        globs.silu_out,
+        globs.logits,
+        globs.pos_id,
+        globs.attn_scale,
+        globs.rms_norm_eps,
+        globs.skip_attn_reduction,
+        stream=torch.cuda.current_stream(),
+        **options,
+    )
+
+
+class LatencyMK_Interpreter(MK_Interpreter):
+    """`options` are passed to every launch (e.g. l2_prefetch_stages)."""
+
+    def __init__(self, mk_dir: Path | str | None = None, **options):
+        super().__init__(mk_dir)
+        self.options = options
+
+    def interpret(self, globs: Globals):
+        interpret_with_mk(globs, self.mk_func, **self.options)
+
+
+class Latency3B_MK_Interpreter(MK_Interpreter):
+    def __init__(self, mk_dir: Path | str | None = None, **options):
+        _add_to_path(mk_dir)
+        from mk_llama_3b import mk_llama_3b  # type: ignore
+
+        self.mk_func = mk_llama_3b
+        self.options = options
+
+    def interpret(self, globs: Globals):
+        interpret_with_mk(globs, self.mk_func, **self.options)

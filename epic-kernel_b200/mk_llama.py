@@ -1,0 +1,173 @@
+"""`mk_llama` / `mk_llama_3b`: drop-in replacements of epic-kernel's pybind
+modules of the same names (demos/low-latency-llama/llama_1b.cu:23-47,
+llama_3b.cu:26-53).
+
+The positional signature is the reference's (megakernels/demos/latency/mk.py:
+18-52): the VM tensors, the weights, the 4-D KV caches, the rotary tables, the
+activation buffers, then pos_id, attn_scale, rms_norm_eps,
+skip_attn_reduction, and `stream=` as a keyword. Unlike the reference, one
+module serves every Llama size, because the model dimensions are read from the
+tensor shapes instead of being compiled in.
+
+Extra keyword-only options (defaults match the reference's behaviour):
+  l2_prefetch_stages  16 KiB weight stages prefetched into L2 ahead of the
+                      shared-memory ring (0 = off)
+  timeout_ns          bound of every cross-SM wait (default 1 s)
+  record_timings      write start / dependency-ready / end stamps (ns) into
+                      timings[q, i, 0..2]
+  down_reduction_size columns per DownProjResidual split (default gcd(I, H),
+                      as the schedule builder uses)
+
+Errors: bad shapes or dtypes raise ValueError before launch; a CUDA launch
+failure raises RuntimeError. Device-side failures (timeouts, malformed
+instructions) are recorded on the device. Call `check()` after synchronising
+to raise them as `megakernels.ek.EngineError`.
+"""
+
+import ctypes
+import math
+
+import torch
+
+from megakernels import ek
+
+_BF16 = torch.bfloat16
+_cache: dict = {}
+
+
+def _need(t: torch.Tensor, name: str, dtype, ndim: int | None = None):
+    if not isinstance(t, torch.Tensor):
+        raise ValueError(f"{name}: expected a tensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise ValueError(f"{name}: must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name}: dtype {t.dtype}, expected {dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: must be contiguous")
+    if ndim is not None and t.dim() != ndim:
+        raise ValueError(f"{name}: {t.dim()}-D, expected {ndim}-D")
+    return t.data_ptr()
+
+
+def _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size):
+    (barriers, instructions, timings, qkv_w, attn_ln_w, o_w, mlp_ln_w, up_w, gate_w, down_w,
+     lm_norm_w, lm_w, k4, v4, cos, sin, hidden, q, attn_out, lse, o_int, silu, logits) = tensors
+    a = ek.EkLlamaArgs()
+    a.barriers = _need(barriers, "barriers", torch.int32, 3)
+    a.instructions = _need(instructions, "instructions", torch.int32, 3)
+    a.timings = _need(timings, "timings", torch.int32, 3) if timings is not None else None
+    a.qkv_weights = _need(qkv_w, "qkv_weights", _BF16, 3)
+    a.attn_ln_weights = _need(attn_ln_w, "attn_ln_weights", _BF16, 2)
+    a.o_weights = _need(o_w, "o_weights", _BF16, 3)
+    a.mlp_ln_weights = _need(mlp_ln_w, "mlp_ln_weights", _BF16, 2)
+    a.up_weights = _need(up_w, "up_weights", _BF16, 3)
+    a.gate_weights = _need(gate_w, "gate_weights", _BF16, 3)
+    a.down_weights = _need(down_w, "down_weights", _BF16, 3)
+    a.lm_head_norm_weights = _need(lm_norm_w, "lm_head_norm_weights", _BF16)
+    a.lm_head_weights = _need(lm_w, "lm_head_weights", _BF16, 2)
+    a.k_cache = _need(k4, "k_cache", _BF16, 4)
+    a.v_cache = _need(v4, "v_cache", _BF16, 4)
+    a.rope_cos = _need(cos, "rope_cos", torch.float32, 2)
+    a.rope_sin = _need(sin, "rope_sin", torch.float32, 2)
+    a.hidden_states = _need(hidden, "hidden_states", _BF16)
+    a.q_post_rope = _need(q, "q_post_rope", _BF16)
+    a.attn_out = _need(attn_out, "attn_out", _BF16)
+    a.attn_lse_intermediates = _need(lse, "attn_lse_intermediates", torch.float32, 2)
+    a.attn_out_intermediates = _need(o_int, "attn_out_intermediates", torch.float32, 3)
+    a.silu_out = _need(silu, "silu_out", _BF16)
+    a.logits = _need(logits, "logits", _BF16)
+
+    L, I, H = up_w.shape
+    D = k4.shape[3]
+    Hkv = k4.shape[2]
+    Hq = lse.shape[0]
+    V = lm_w.shape[0]
+    checks = [
+        (qkv_w.shape == (L, (Hq + 2 * Hkv) * D, H), "qkv_weights shape"),
+        (o_w.shape == (L, H, Hq * D), "o_weights shape"),
+        (gate_w.shape == up_w.shape, "gate_weights shape"),
+        (down_w.shape == (L, H, I), "down_weights shape"),
+        (attn_ln_w.shape == (L, H) and mlp_ln_w.shape == (L, H), "layernorm weight shapes"),
+        (lm_norm_w.numel() == H and lm_w.shape[1] == H, "lm head shapes"),
+        (k4.shape[0] == L and v4.shape == k4.shape, "kv cache shapes"),
+        (cos.shape[1] == D and sin.shape == cos.shape, "rope table shapes"),
+        (hidden.numel() == H and q.numel() == Hq * D and attn_out.numel() == Hq * D, "activation sizes"),
+        (o_int.shape[0] == Hq and o_int.shape[1] == lse.shape[1] and o_int.shape[2] == D, "attention intermediates"),
+        (silu.numel() == I and logits.numel() == V, "silu_out / logits sizes"),
+        (barriers.shape[0] == L, "barriers first dim"),
+        (instructions.shape[2] == 32, "instructions last dim"),
+        (timings is None or timings.shape[:2] == instructions.shape[:2], "timings shape"),
+    ]
+    for ok, what in checks:
+        if not ok:
+            raise ValueError(f"mk_llama: inconsistent {what}")
+    devices = {t.device for t in tensors if t is not None}
+    if len(devices) != 1:
+        raise ValueError(f"mk_llama: tensors on several devices {devices}")
+
+    a.num_layers, a.hidden, a.intermediate, a.head_dim = L, H, I, D
+    a.num_q_heads, a.num_kv_heads, a.vocab = Hq, Hkv, V
+    a.kv_len = k4.shape[1]
+    a.rope_rows = cos.shape[0]
+    a.max_partials = lse.shape[1]
+    a.barrier_rows, a.barrier_cols = barriers.shape[1], barriers.shape[2]
+    a.num_queues, a.queue_len = instructions.shape[0], instructions.shape[1]
+    a.down_reduction_size = down_reduction_size or math.gcd(I, H)
+    a.oproj_reduction_size = H
+    a.l2_prefetch_stages = l2_prefetch_stages
+    a.record_timings = int(bool(record_timings))
+    a.timeout_ns = int(timeout_ns)
+    return a, next(iter(devices)).index
+
+
+def mk_llama(
+    barriers, instructions, timings,
+    qkv_proj_weights, attn_ln_weights, o_proj_weights, mlp_ln_weights,
+    up_proj_weights, gate_proj_weights, down_proj_weights,
+    lm_head_norm_weights, lm_head_weights,
+    k_cache, v_cache, rope_cos, rope_sin,
+    hidden_states, post_ln_rope_q, attn_out, attn_lse_intermediates, attn_out_intermediates,
+    silu_out, logits,
+    pos_id, attn_scale, rms_norm_eps, skip_attn_reduction,
+    *, stream=None, l2_prefetch_stages: int = 0, record_timings: bool = False,
+    timeout_ns: int = 0, down_reduction_size: int = 0,
+):
+    tensors = (barriers, instructions, timings, qkv_proj_weights, attn_ln_weights, o_proj_weights,
+               mlp_ln_weights, up_proj_weights, gate_proj_weights, down_proj_weights,
+               lm_head_norm_weights, lm_head_weights, k_cache, v_cache, rope_cos, rope_sin,
+               hidden_states, post_ln_rope_q, attn_out, attn_lse_intermediates,
+               attn_out_intermediates, silu_out, logits)
+    key = (tuple((t.data_ptr(), tuple(t.shape), t.dtype) if t is not None else None for t in tensors),
+           l2_prefetch_stages, bool(record_timings), int(timeout_ns), down_reduction_size)
+    hit = _cache.get(key)
+    if hit is None:
+        hit = _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size)
+        if len(_cache) > 64:
+            _cache.clear()
+        _cache[key] = hit
+    args, device = hit
+    args.pos_id = int(pos_id)
+    args.attn_scale = float(attn_scale)
+    args.rms_norm_eps = float(rms_norm_eps)
+    args.skip_attn_reduction = int(bool(skip_attn_reduction))
+    ctx = ek.context_for(device)
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    handle = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+    ek.check(
+        ek.load_library().ek_llama_decode(ctx.handle, ctypes.byref(args), ctypes.c_void_p(handle)),
+        "ek_llama_decode",
+    )
+
+
+def check(device: int | None = None, clear: bool = True):
+    """Synchronise and raise `EngineError` if a launch recorded a device failure."""
+    if device is None:
+        device = torch.cuda.current_device()
+    ek.context_for(device).raise_if_failed(clear)
+
+
+def read_status(device: int | None = None, clear: bool = False) -> dict:
+    if device is None:
+        device = torch.cuda.current_device()
+    return ek.context_for(device).read_status(clear).as_dict()

@@ -1,0 +1,133 @@
+/*
+ * ek.h - C ABI of the B200 batch-1 decode megakernel.
+ *
+ * One call runs one decode step: a single persistent kernel on the caller's
+ * stream interprets the per-SM instruction queues built by the Python
+ * scheduler. Every buffer is caller-owned device memory passed as a plain
+ * pointer. The call is asynchronous, and it allocates nothing once the
+ * context's scratch has grown to the model's size (the first call on a
+ * context allocates it).
+ *
+ * Errors: a nonzero return is a host-side rejection (bad argument, CUDA launch
+ * failure); ek_last_error() describes it. Device-side failures (a cross-SM wait
+ * that timed out, a malformed instruction) do not stop the host. The kernel
+ * records the first one in the context's status record and drains its queues
+ * without further writes. ek_read_status() returns that record.
+ */
+#ifndef EK_H_
+#define EK_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EK_ABI_VERSION 1
+
+/* host return codes */
+#define EK_SUCCESS 0
+#define EK_E_INVALID 1   /* bad pointer, shape, alignment or size */
+#define EK_E_CUDA 2      /* a CUDA runtime call failed */
+#define EK_E_UNSUPPORTED 3
+
+/* device status codes (EkStatus.code) */
+#define EK_STATUS_OK 0
+#define EK_STATUS_TIMEOUT 1         /* a cross-SM counter wait ran out of time */
+#define EK_STATUS_BAD_OPCODE 2      /* opcode not defined for this model */
+#define EK_STATUS_BAD_INSTRUCTION 3 /* a field of an instruction is out of range */
+#define EK_STATUS_RING_TIMEOUT 4    /* internal load ring stalled (engine bug) */
+
+typedef struct EkContext EkContext;
+
+/* First device-side failure since the status was last cleared. */
+typedef struct EkStatus {
+  int32_t code;     /* EK_STATUS_* */
+  int32_t sm;       /* queue (thread block) that recorded it */
+  int32_t instr;    /* index of the instruction in that queue */
+  int32_t opcode;
+  int32_t layer;
+  int32_t observed; /* counter value last seen (timeouts) */
+  int32_t expected; /* counter value waited for (timeouts) / bad word index */
+  int32_t detail;   /* barrier slot (timeouts) / offending word value */
+} EkStatus;
+
+/*
+ * Arguments of one Llama decode step. The fields are the tensors of
+ * `mk_llama(...)`, in the same order (megakernels/demos/latency/mk.py:18-52 and
+ * demos/low-latency-llama/llama_1b.cu:23-46 in epic-kernel), plus the model
+ * dimensions that the reference compiles into separate binaries.
+ * All weights and activations are bf16 unless marked f32.
+ */
+typedef struct EkLlamaArgs {
+  int32_t* barriers;           /* [L, barrier_rows, barrier_cols] int32, zeroed by the caller */
+  const int32_t* instructions; /* [num_queues, queue_len, 32] int32 */
+  int32_t* timings;            /* [num_queues, queue_len, 128] int32, or NULL */
+  const void* qkv_weights;     /* [L, (Hq + 2 Hkv) D, H] */
+  const void* attn_ln_weights; /* [L, H] */
+  const void* o_weights;       /* [L, H, Hq D] */
+  const void* mlp_ln_weights;  /* [L, H] */
+  const void* up_weights;      /* [L, I, H] */
+  const void* gate_weights;    /* [L, I, H] */
+  const void* down_weights;    /* [L, H, I] */
+  const void* lm_head_norm_weights; /* [H] */
+  const void* lm_head_weights; /* [V, H] */
+  void* k_cache;               /* [L, kv_len, Hkv, D] */
+  void* v_cache;               /* [L, kv_len, Hkv, D] */
+  const float* rope_cos;       /* f32 [rope_rows, D], interleaved pair layout */
+  const float* rope_sin;       /* f32 [rope_rows, D] */
+  void* hidden_states;         /* [H] */
+  void* q_post_rope;           /* [Hq D] */
+  void* attn_out;              /* [Hq D] */
+  float* attn_lse_intermediates; /* f32 [Hq, max_partials] */
+  float* attn_out_intermediates; /* f32 [Hq, max_partials, D] */
+  void* silu_out;              /* [I] */
+  void* logits;                /* [V] */
+
+  int32_t num_layers, hidden, intermediate, head_dim, num_q_heads, num_kv_heads, vocab;
+  int32_t kv_len;        /* cache rows per layer */
+  int32_t rope_rows;     /* rows of rope_cos / rope_sin */
+  int32_t max_partials;  /* second dim of the attention intermediates */
+  int32_t barrier_rows, barrier_cols;
+  int32_t num_queues, queue_len;
+
+  int32_t pos_id;
+  float attn_scale;
+  float rms_norm_eps;
+  int32_t skip_attn_reduction;
+
+  int32_t down_reduction_size;  /* columns of W_down per DownProjResidual split (gcd(I, H)) */
+  int32_t oproj_reduction_size; /* columns of W_o per O_ProjResidual split (H) */
+  int32_t l2_prefetch_stages;   /* 16 KiB weight stages prefetched into L2 beyond the ring; 0 = off */
+  int32_t record_timings;       /* write timings[q, i, 0..2] when timings != NULL */
+  int64_t timeout_ns;           /* bound of every cross-SM wait; <= 0 selects 1 s */
+} EkLlamaArgs;
+
+/* ABI version compiled into the library (EK_ABI_VERSION). */
+int ek_abi_version(void);
+
+/* Message of the last failing host call on this thread ("" if none). */
+const char* ek_last_error(void);
+
+/* Create a context on `device` (status record, scratch). One decode step at a
+ * time per context. */
+int ek_context_create(int device, EkContext** out);
+void ek_context_destroy(EkContext* ctx);
+
+/*
+ * Llama-3.2 1B / 3B decode step. Replaces the pybind entry points `mk_llama`
+ * and `mk_llama_3b` of epic-kernel (demos/low-latency-llama/llama_1b.cu:23-47,
+ * llama_3b.cu:26-53; called from megakernels/demos/latency/mk.py:11-52).
+ * `stream` is a cudaStream_t (NULL = legacy default stream).
+ */
+int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* args, void* stream);
+
+/* Copy the device status record to `out` (synchronises with all work queued
+ * on the context's device). With `clear`, reset it to EK_STATUS_OK. */
+int ek_read_status(EkContext* ctx, EkStatus* out, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EK_H_ */
