@@ -1,0 +1,382 @@
+"""Batch-1 decode benchmark: Llama-3.2-1B (random-init bf16) at KV length 2048.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--kv 2048] [--model 1b|3b] [--prefetch S]
+
+A step is one decode token: embed, barrier reset, one megakernel launch over
+the whole model, argmax. The output token feeds the next step, as in
+MK_Generator.generate. Weights (2.47 GB) are far larger than L2 (126 MB), so
+no L2 flush is needed between steps.
+
+One JSON line is printed by rank 0:
+- `value`: tokens/s with all inputs resident in HBM (device-timed, CUDA events,
+  max over ranks). For N > 1 each rank runs an independent replica, so the
+  scaling is weak and `value` sums over ranks.
+- `e2e`: the same metric through the public API with host buffers. Every step
+  copies the input token from pinned host memory and reads the output token
+  back to the host.
+- `roofline`: HBM-bound. `achieved` is the algorithmic bytes per launch
+  (weights read once + KV rows read) over the mean megakernel launch time,
+  and `peak` is MEASURED_PEAKS.json hbm_gbs.
+- `cpu_baseline`: the CPU oracle (a port of the reference's PyVM) timed on a
+  bounded sample on this host.
+
+`--impl reference` times the reference's CPU interpreter path (the oracle
+port; the reference's CUDA megakernel cannot be built because its
+ThunderKittens dependency is not vendored) on the same workload and metric.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT / "epic-kernel_b200", ROOT, ROOT / "tests" / "golden"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+import torch  # noqa: E402
+
+METRIC = "batch-1 decode tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kv", type=int, default=2048)
+    ap.add_argument("--model", default="1b", choices=["1b", "3b"])
+    ap.add_argument("--prefetch", type=int, default=0, help="L2 prefetch stages (0 = off)")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def model_config(name):
+    from megakernels.llama import llama_3_2_1b_config, llama_3_2_3b_config
+
+    return llama_3_2_1b_config() if name == "1b" else llama_3_2_3b_config()
+
+
+def build_model(name, max_len, device):
+    from megakernels.llama import LlamaForCausalLM
+    from megakernels.model_types import ExtraModelConfig
+
+    return LlamaForCausalLM.random_init(
+        model_config(name), ExtraModelConfig(interleave_rope=True, max_len_override=max_len),
+        seed=0, device=device)
+
+
+def weight_bytes(model) -> int:
+    sp = model.stacked_params
+    mats = [sp.qkv_proj, sp.o_proj, sp.up_proj, sp.gate_proj, sp.down_proj, model.lm_head.lm_head.weight]
+    return sum(t.numel() * t.element_size() for t in mats)
+
+
+def kv_bytes_per_token(model) -> int:
+    c = model.config
+    return c.num_hidden_layers * 2 * c.num_key_value_heads * c.head_dim * 2
+
+
+def fill_kv(model, kv):
+    from megakernels.synthetic import seeded_normal
+
+    k, v = model.stacked_kv_cache
+    L, B, _, H, D = k.shape
+    for i, c in enumerate((k, v)):
+        c[:, :, :kv] = seeded_normal((L, B, kv, H, D), 1, 7000 + i).to(c.device)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def read_profile_traffic(workload):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    f = ROOT / "profiles" / f"decode_kernel_{workload}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1].strip()))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.15)
+            self.proc.terminate()
+            out, _ = self.proc.communicate(timeout=5)
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def cpu_decode_sample(name, kv, tokens):
+    """Time `tokens` decode steps of the CPU oracle (a port of the reference
+    PyVM) at KV length `kv`. Returns (tokens/s, threads, seconds)."""
+    from megakernels.demos.latency.scheduler import LatencyScheduleBuilder
+    from oracle import pyvm
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    model = build_model(name, kv + tokens + 1, "cpu")
+    fill_kv(model, kv)
+    sched = LatencyScheduleBuilder.build(model, seq_len=kv + tokens)
+    instrs = sched.get_linear_instructions()
+    tok = 0
+    with torch.no_grad():
+        pyvm.pyvm_step(model, sched.globs, instrs, tok, kv - 1)  # warm-up (not timed)
+        t0 = time.perf_counter()
+        for i in range(tokens):
+            _, tok = pyvm.pyvm_step(model, sched.globs, instrs, tok, kv + i)
+        dt = time.perf_counter() - t0
+    return tokens / dt, torch.get_num_threads(), dt
+
+
+def dist_setup(n):
+    if n <= 1 and "RANK" not in os.environ:
+        return 0, 1, 0
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", n))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29511")
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", local))
+    else:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+    return rank, world, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    samples = max(1, min(args.steps, args.cpu_sample_tokens))
+    tps, cores, dt = cpu_decode_sample(args.model, args.kv, samples)
+    workload = f"llama-3.2-{args.model}-kv{args.kv}-decode"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": samples, "warmup": 1, "ms_per_step": 1000.0 / tps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02) seed 0; KV N(0,1) seed 1)",
+        "config": {"workload": workload, "kv_len": args.kv, "batch": 1},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{samples} decode token(s) of the full model at KV {args.kv}, "
+                                   f"{dt:.1f} s, CPU port of the reference PyVM (reference CUDA "
+                                   f"megakernel unbuildable: ThunderKittens not vendored)"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    import mk_llama
+    from megakernels.demos.latency.mk import LatencyMK_Interpreter
+    from megakernels.demos.latency.scheduler import LatencyScheduleBuilder
+    from megakernels.generators import MK_Generator
+    from megakernels.scheduler import assign_to_sms, tensorize_instructions
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    total = args.warmup + args.steps
+    max_len = args.kv + 2 * total + 16
+    model = build_model(args.model, max_len, dev)
+    fill_kv(model, args.kv)
+    sched = LatencyScheduleBuilder.build(model, seq_len=args.kv + 2 * total)
+    tensorize_instructions(sched.globs, assign_to_sms("rr", schedule=sched))
+    interp = LatencyMK_Interpreter(l2_prefetch_stages=args.prefetch)
+    gen = MK_Generator(model, interp, sched)
+    stream = torch.cuda.current_stream(dev)
+    g = sched.globs
+    emb = model.model.embed_tokens.embed_tokens.weight
+
+    tok = torch.zeros(1, 1, dtype=torch.long, device=dev)
+    pos = args.kv
+    with torch.no_grad():
+        # ---- device-resident leg: tokens stay on the GPU
+        for _ in range(args.warmup):
+            tok = gen.run(tok, pos).view(1, 1)
+            pos += 1
+        torch.cuda.synchronize()
+        mk_llama.check(local)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        kv_lens = []
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            t_start.record(stream)
+            for i in range(args.steps):
+                g.hidden_states[:] = emb[tok.view(-1)].view(-1)
+                gen.fill()
+                g.pos_id = pos
+                g.logits.zero_()
+                starts[i].record(stream)
+                interp.interpret(g)
+                ends[i].record(stream)
+                tok = torch.argmax(g.logits, dim=-1).view(1, 1)
+                kv_lens.append(pos + 1)
+                pos += 1
+            t_end.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        mk_llama.check(local)
+        step_ms = t_start.elapsed_time(t_end) / args.steps
+        kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+        # ---- end-to-end leg through the public API with host buffers
+        h_in = torch.zeros(1, 1, dtype=torch.long).pin_memory()
+        h_out = torch.zeros(1, dtype=torch.long).pin_memory()
+        d_in = torch.zeros(1, 1, dtype=torch.long, device=dev)
+
+        def e2e_step(p):
+            d_in.copy_(h_in, non_blocking=True)
+            h_out.copy_(gen.run(d_in, p).view(-1), non_blocking=True)
+            stream.synchronize()
+            h_in[0, 0] = h_out[0]  # the host reads the result before the next step
+
+        for _ in range(2):
+            e2e_step(pos)
+            pos += 1
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step(pos)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        mk_llama.check(local)
+
+    step_ms = max_over_ranks(step_ms, world)
+    e2e_ms = max_over_ranks(e2e_ms, world)
+    mean_kernel_ms = statistics.mean(kernel_ms)
+    alg_bytes = weight_bytes(model) + kv_bytes_per_token(model) * statistics.mean(kv_lens)
+    peak, peak_kind = load_peaks()
+    achieved = alg_bytes / (mean_kernel_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        del model, sched, gen
+        tps, cores, dt = cpu_decode_sample(args.model, args.kv, args.cpu_sample_tokens)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{args.cpu_sample_tokens} decode tokens of the full model at KV {args.kv} "
+                         f"through the CPU port of the reference PyVM ({dt:.1f} s)"}
+    if rank != 0:
+        return
+    workload = f"llama-3.2-{args.model}-kv{args.kv}-decode"
+    line = {
+        "metric": METRIC, "value": world * 1000.0 / step_ms, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights N(0,0.02) seed 0; KV N(0,1) seed 1)",
+        "config": {"workload": workload, "kv_len": args.kv, "batch": 1,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2_prefetch_stages": args.prefetch,
+                   "l2": "no flush: 2.5 GB of weights per step >> 126 MB L2"},
+        "gpu_launches": args.steps,
+        "ms_per_token_kernel": mean_kernel_ms,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "traffic": read_profile_traffic(workload)},
+        "clocks": clocks.summary(),
+        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tokens/s",
+                "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

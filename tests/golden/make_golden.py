@@ -30,7 +30,7 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "epic-kernel_b200"))
 
-from megakernels.llama import LlamaConfig, LlamaForCausalLM  # noqa: E402
+from megakernels.llama import LlamaConfig, LlamaForCausalLM, llama_3_2_1b_config  # noqa: E402
 from megakernels.model_types import ExtraModelConfig  # noqa: E402
 from megakernels.synthetic import seeded_normal, seeded_randint  # noqa: E402
 
@@ -155,7 +155,6 @@ def run_tiny(ref, out: dict):
 
 
 def run_1b_greedy(ref, out: dict, prompt_len=128, ntok=64):
-    from megakernels.llama import llama_3_2_1b_config
 
     max_len = 256
     mine = LlamaForCausalLM.random_init(

@@ -1,0 +1,135 @@
+"""GPU parity of the Llama decode megakernel (through mk_llama -> libek.so).
+
+Bar: barrier counters bit-exact; logits within max(2e-2 x std, 2 x noise
+floor) of the reference interpreter's, where the noise floor is the
+difference between the reference interpreter and the same interpreter with a
+different fp32 summation order (gpu_helpers.noise_floor). Intermediate bf16
+activations may differ by about a bf16 ulp where the fp32 summation order moves
+a dot product across a rounding boundary (about 3 in 10^4 outputs).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from gpu_helpers import (
+    assert_logits_within_floor, bf16_from_bits, noise_floor, prepare, run_gpu, ulp_diff,
+)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny_gpu():
+    assert torch.cuda.is_available()
+    return cases.tiny_model("cuda")
+
+
+@pytest.fixture(scope="module")
+def tiny_cpu():
+    return cases.tiny_model("cpu")
+
+
+@pytest.fixture(scope="module")
+def golden(golden_dir):
+    return np.load(golden_dir / "llama_tiny_step.npz")
+
+
+def assert_close_bf16(mine, ref, name, max_frac=0.02):
+    """At most `max_frac` of the elements differ, and each difference is within
+    two bf16 ulps of the element plus 2e-2 x std (cancellation in residual adds
+    can leave a tiny value with a large ulp distance)."""
+    mine = mine.detach().cpu().to(torch.bfloat16).reshape(-1)
+    ref = ref.detach().cpu().to(torch.bfloat16).reshape(-1)
+    frac = (ulp_diff(mine, ref) > 0).float().mean().item()
+    assert frac <= max_frac, f"{name}: {frac:.3%} of elements differ"
+    r = ref.float()
+    ulp = torch.exp2(torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
+    bound = 2 * ulp + 2e-2 * r.std()
+    excess = ((mine.float() - r).abs() - bound).max().item()
+    assert excess <= 0, f"{name}: error exceeds bound by {excess}"
+
+
+@pytest.mark.parametrize("pos", cases.TINY_POSITIONS)
+def test_tiny_step_vs_reference_interpreter(tiny_gpu, tiny_cpu, golden, pos):
+    hidden = cases.step_hidden(2048, pos)
+    sched = prepare(tiny_gpu, pos, hidden)
+    run_gpu(sched)
+    import mk_llama
+
+    mk_llama.check()
+    g = sched.globs
+    np.testing.assert_array_equal(g.barriers.cpu().numpy(), golden[f"p{pos}_barriers"])
+    ref_logits = bf16_from_bits(golden[f"p{pos}_logits"])
+    _, alt = noise_floor(tiny_cpu, pos, hidden)
+    assert_logits_within_floor(g.logits, ref_logits, alt.globs.logits)
+    for name in ("post_ln_rope_q", "attn_out", "silu_out", "hidden_states"):
+        assert_close_bf16(getattr(g, name), bf16_from_bits(golden[f"p{pos}_{name}"]), name)
+    assert_close_bf16(g.k_cache[:, 0, pos], bf16_from_bits(golden[f"p{pos}_k_row"]), "k row")
+    assert_close_bf16(g.v_cache[:, 0, pos], bf16_from_bits(golden[f"p{pos}_v_row"]), "v row")
+    # rows past pos keep their poison (no stray writes)
+    assert g.k_cache[:, 0, pos + 1 :].float().abs().max() > 50
+
+
+@pytest.mark.parametrize("stop", ["qkv", "partial", "oproj", "upgate", "downproj"])
+def test_one_layer_stages_vs_oracle(tiny_gpu, tiny_cpu, stop):
+    """Each stage of layer 0 alone (stop_after_op, as diff_test.py does)."""
+    from gpu_helpers import run_oracle
+
+    pos = 777
+    hidden = cases.step_hidden(2048, pos)
+    ref = prepare(tiny_cpu, pos, hidden, layer_limit=1, stop_after_op=stop)
+    s = prepare(tiny_gpu, pos, hidden, layer_limit=1, stop_after_op=stop)
+    run_gpu(s)
+    import mk_llama
+
+    mk_llama.check()
+    run_oracle(ref)
+    assert torch.equal(s.globs.barriers.cpu(), ref.globs.barriers)
+    for n in ("post_ln_rope_q", "attn_out", "silu_out", "hidden_states"):
+        assert_close_bf16(getattr(s.globs, n), getattr(ref.globs, n), n, max_frac=0.005)
+    for n in ("attn_lse_intermediates", "attn_out_intermediates"):
+        a, b = getattr(s.globs, n).cpu(), getattr(ref.globs, n)
+        assert (a - b).abs().max().item() <= 1e-5, n
+
+
+@pytest.mark.parametrize("mode", ["zz", "wave", "dag"])
+def test_assignment_policies_are_bitwise_identical(tiny_gpu, mode):
+    pos = 300
+    a = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
+    run_gpu(a, "rr")
+    ref = {n: getattr(a.globs, n).clone() for n in ("hidden_states", "logits", "attn_out", "barriers")}
+    b = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
+    run_gpu(b, mode)
+    for n, t in ref.items():
+        assert torch.equal(getattr(b.globs, n), t), f"{n} differs between rr and {mode}"
+
+
+def test_repeat_runs_deterministic(tiny_gpu):
+    pos = 777
+    outs = []
+    for _ in range(3):
+        s = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
+        run_gpu(s, "rr", l2_prefetch_stages=16)
+        outs.append((s.globs.hidden_states.clone(), s.globs.logits.clone()))
+    for h, l in outs[1:]:
+        assert torch.equal(h, outs[0][0]) and torch.equal(l, outs[0][1])
+
+
+def test_l2_prefetch_does_not_change_results(tiny_gpu):
+    pos = 300
+    a = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
+    run_gpu(a, l2_prefetch_stages=0)
+    b = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
+    run_gpu(b, l2_prefetch_stages=32)
+    assert torch.equal(a.globs.logits, b.globs.logits)
+
+
+def test_timings_recorded(tiny_gpu):
+    pos = 5
+    s = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
+    run_gpu(s, record_timings=True)
+    t = s.globs.timings
+    real = s.globs.instructions[:, :, 0] != 0
+    assert bool((t[:, :, 2][real] != 0).all())
