@@ -19,7 +19,10 @@ struct Consumer {
   int* flag;        // one int broadcast between consumer threads
   int tid, warp, lane;
   int qidx, iidx;   // queue and instruction index (error reports, timings)
-  bool broken;      // the ring stalled: leave the kernel
+  // The ring stalled (an engine bug, reported as EK_STATUS_RING_TIMEOUT). A
+  // broken warp stops waiting on the ring but keeps the same control flow, so
+  // every named barrier is still reached by all consumer warps.
+  bool broken;
 
   __device__ Consumer(const KParams& p_) : p(p_) {}
 
@@ -27,9 +30,12 @@ struct Consumer {
 
   // Wait for stage data; every consumer warp calls this for every stage.
   __device__ __forceinline__ const uint8_t* acquire() {
-    if (!ring_wait(&ring.full[ring.slot], ring.phase, 4 * p.timeout_ns + 2000000000ll)) {
-      if (lane == 0) record_error(p, 4, iidx, -1, -1, ring.slot, (int)ring.phase, warp);
-      broken = true;
+    if (!broken) {
+      const bool ok = ring_wait(&ring.full[ring.slot], ring.phase, 4 * p.timeout_ns + 2000000000ll);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) record_error(p, 4, iidx, -1, -1, ring.slot, (int)ring.phase, warp);
+        broken = true;
+      }
     }
     return ring.stages + (size_t)ring.slot * STAGE_BYTES;
   }
@@ -41,7 +47,7 @@ struct Consumer {
   }
 
   __device__ void drain(int ns) {
-    for (int k = 0; k < ns && !broken; ++k) {
+    for (int k = 0; k < ns; ++k) {
       acquire();
       release();
     }
@@ -171,7 +177,6 @@ struct Consumer {
     float a0 = 0.f, a1 = 0.f;
     for (int s = 0; s < spb; ++s) {
       const uint8_t* st = acquire();
-      if (broken) return;
       mac_stage(st, s * GEMV_STAGE_COLS, s * GEMV_STAGE_COLS + 256 < K, a0, a1);
       release();
     }
@@ -187,17 +192,17 @@ struct Consumer {
       int* a = bar(l - 1, OP_DOWN - 1, 0);
       const int t = p.down_splits * (p.H / 16);
       if (!wait_counters(1, &a, &t, OP_QKV, l)) { drain(pl.ns); return; }
-    } else if (aborted(p)) {
+    } else if (!wait_counters(0, nullptr, nullptr, OP_QKV, l)) {  // abort check, CTA-uniform
       drain(pl.ns);
       return;
     }
     stamp(1);
     rmsnorm_to_act(p.hidden, p.attn_ln + (size_t)l * p.H, p.H);
+    stamp(3);
     const int qdim = p.Hq * p.D, kdim = p.Hkv * p.D;
     for (int b = b0; b < b1; ++b) {
       float r0, r1;
       gemv_block(p.H, r0, r1);
-      if (broken) return;
       if (lane == 0) {
         const int row = b * 16 + 2 * warp;  // even: rows (row, row + 1) form a rotary pair
         float v0 = bf16r(r0), v1 = bf16r(r1);
@@ -237,49 +242,72 @@ struct Consumer {
     }
   }
 
-  // Per-lane dims of one KV row: D / 32 consecutive elements.
-  template <int D>
-  __device__ __forceinline__ void load_row(const __nv_bfloat16* src, float* out, bool global) {
-    constexpr int DPL = D / 32;
-    if constexpr (DPL == 2) {
-      const uint32_t u = global ? __ldcg(reinterpret_cast<const unsigned*>(src) + lane)
-                                : reinterpret_cast<const uint32_t*>(src)[lane];
-      out[0] = bf_lo(u);
-      out[1] = bf_hi(u);
+  // Attention keeps one lane group per token: a warp holds TPW tokens of a
+  // ring stage, LPT = 32 / TPW lanes per token, 16 head dims per lane. Scores
+  // need a LPT-lane reduction, and the online-softmax update runs once per
+  // tile of TPW tokens (warp-wide max / sum), not once per token.
+  __device__ __forceinline__ static void load16(const __nv_bfloat16* src, float* out, bool global) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4 a, b;
+    if (global) {
+      a = __ldcg(s4);
+      b = __ldcg(s4 + 1);
     } else {
-      const uint2 u = global ? __ldcg(reinterpret_cast<const uint2*>(src) + lane)
-                             : reinterpret_cast<const uint2*>(src)[lane];
-      out[0] = bf_lo(u.x);
-      out[1] = bf_hi(u.x);
-      out[2] = bf_lo(u.y);
-      out[3] = bf_hi(u.y);
+      a = s4[0];
+      b = s4[1];
+    }
+    const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      out[2 * k] = bf_lo(u[k]);
+      out[2 * k + 1] = bf_hi(u[k]);
     }
   }
 
-  template <int D>
-  struct AttnState {
-    float q[MAX_GQA][D / 32];
-    float m[MAX_GQA], l[MAX_GQA];
-    float acc[MAX_GQA][D / 32];
-  };
-
-  template <int D>
-  __device__ __forceinline__ void attend(AttnState<D>& s, const float* k, const float* v, int gqa) {
-    constexpr int DPL = D / 32;
+  // One tile: this lane's token row (k, v point at the lane's 16 dims), `valid`
+  // per lane group. All 32 lanes must call it.
+  template <int LPT>
+  __device__ __forceinline__ void attend_tile(const float* q,
+                                              float (&acc)[MAX_GQA][16], float* m, float* l,
+                                              const __nv_bfloat16* k, const __nv_bfloat16* v,
+                                              bool valid, bool global, int gqa) {
+    float kv[16], vv[16];
+    if (valid) {
+      load16(k, kv, global);
+      load16(v, vv, global);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) kv[e] = vv[e] = 0.f;
+    }
 #pragma unroll
     for (int h = 0; h < MAX_GQA; ++h) {
       if (h >= gqa) break;
       float d = 0.f;
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) d = fmaf(s.q[h][e], k[e], d);
-      const float sc = warp_sum(d) * p.scale;
-      const float mn = fmaxf(s.m[h], sc);
-      const float corr = expf(s.m[h] - mn);
-      const float pe = expf(sc - mn);
-      s.l[h] = s.l[h] * corr + pe;
+      for (int e = 0; e < 16; e += 4) {
+        const float4 qq = *reinterpret_cast<const float4*>(q + h * 128 + e);
+        d = fmaf(qq.x, kv[e], d);
+        d = fmaf(qq.y, kv[e + 1], d);
+        d = fmaf(qq.z, kv[e + 2], d);
+        d = fmaf(qq.w, kv[e + 3], d);
+      }
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) s.acc[h][e] = fmaf(pe, v[e], s.acc[h][e] * corr);
-      s.m[h] = mn;
+      for (int o = 1; o < LPT; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+      const float sc = valid ? d * p.scale : -INFINITY;
+      float mt = sc;
+#pragma unroll
+      for (int o = LPT; o < 32; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mn = fmaxf(m[h], mt);
+      const float mref = mn == -INFINITY ? 0.f : mn;
+      const float corr = expf(m[h] - mref);
+      const float pe = valid ? expf(sc - mref) : 0.f;
+      float ps = pe;
+#pragma unroll
+      for (int o = LPT; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l[h] = l[h] * corr + ps;
+      m[h] = mn;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc[h][e] = fmaf(pe, vv[e], acc[h][e] * corr);
     }
   }
 
@@ -288,7 +316,10 @@ struct Consumer {
   // log2(sum(exp(scores))).
   template <int D>
   __device__ void op_partial(const Ins& ins, const Plan& pl) {
-    constexpr int DPL = D / 32;
+    constexpr int TK = HALF_STAGE / (D * 2);  // tokens per stage
+    constexpr int TPW = TK / CW;              // tokens per warp per stage
+    constexpr int LPT = 32 / TPW;             // lanes per token
+    static_assert(LPT * 16 == D, "16 dims per lane");
     const int l = ins.w[1], kvh = ins.w[2], P = ins.w[3], part = ins.w[4];
     const int gqa = p.gqa, hs = kvh * gqa, bph = D / 16;
     {
@@ -302,50 +333,61 @@ struct Consumer {
     }
     stamp(1);
     const TokenRange tr = partial_tokens(p, P, part);
-    AttnState<D> s;
+    const int grp = lane / LPT, sub = lane % LPT;
+    // q of the group's heads, fp32, in shared memory: qs[h * 128 + d]
+    float* qs = reinterpret_cast<float*>(act + 24576);
+    for (int i = tid; i < gqa * D; i += NC)
+      qs[(i / D) * 128 + i % D] = ldcg_bf16(p.q + (size_t)hs * D + i);
+    sync();
+    const float* q = qs + sub * 16;
+    stamp(3);
+    float acc[MAX_GQA][16], m[MAX_GQA], lsum[MAX_GQA];
 #pragma unroll
     for (int h = 0; h < MAX_GQA; ++h) {
-      s.m[h] = -INFINITY;
-      s.l[h] = 0.f;
+      m[h] = -INFINITY;
+      lsum[h] = 0.f;
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) s.acc[h][e] = 0.f;
-      if (h < gqa) load_row<D>(p.q + (size_t)(hs + h) * D, s.q[h], true);
+      for (int e = 0; e < 16; ++e) acc[h][e] = 0.f;
     }
-    const int kvrow = p.Hkv * D;
     for (int k = 0; k < pl.ns; ++k) {
       const uint8_t* st = acquire();
-      if (broken) return;
-      const int t0 = tr.t_begin + k * p.tk;
-      for (int j = warp; j < p.tk; j += CW) {
-        if (t0 + j >= tr.t_load_end) break;
-        float kv[DPL], vv[DPL];
-        load_row<D>(reinterpret_cast<const __nv_bfloat16*>(st + j * D * 2), kv, false);
-        load_row<D>(reinterpret_cast<const __nv_bfloat16*>(st + HALF_STAGE + j * D * 2), vv, false);
-        attend<D>(s, kv, vv, gqa);
-      }
+      const int j = warp * TPW + grp;
+      const bool valid = tr.t_begin + k * TK + j < tr.t_load_end;
+      const __nv_bfloat16* kr = reinterpret_cast<const __nv_bfloat16*>(st + j * D * 2) + sub * 16;
+      const __nv_bfloat16* vr = reinterpret_cast<const __nv_bfloat16*>(st + HALF_STAGE + j * D * 2) + sub * 16;
+      attend_tile<LPT>(q, acc, m, lsum, kr, vr, valid, false, gqa);
       release();
     }
     // the token appended by this step's QKV instructions is read from global
     if (warp == 0 && p.pos >= tr.t_begin && p.pos < tr.t_end) {
-      float kv[DPL], vv[DPL];
-      const size_t off = ((size_t)l * p.T + p.pos) * kvrow + (size_t)kvh * D;
-      load_row<D>(p.k_cache + off, kv, true);
-      load_row<D>(p.v_cache + off, vv, true);
-      attend<D>(s, kv, vv, gqa);
+      const size_t off = ((size_t)l * p.T + p.pos) * (p.Hkv * D) + (size_t)kvh * D + sub * 16;
+      attend_tile<LPT>(q, acc, m, lsum, p.k_cache + off, p.v_cache + off, grp == 0, true, gqa);
+    }
+    stamp(4);
+    // sum each lane's V accumulator over the warp's token groups
+#pragma unroll
+    for (int h = 0; h < MAX_GQA; ++h) {
+      if (h >= gqa) break;
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+#pragma unroll
+        for (int o = LPT; o < 32; o <<= 1) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
     }
     // merge the per-warp online-softmax states
-    float* mm = reinterpret_cast<float*>(act);          // [CW][gqa]
-    float* ll = mm + CW * MAX_GQA;                      // [CW][gqa]
-    float* aa = ll + CW * MAX_GQA;                      // [CW][gqa][D]
+    float* mm = reinterpret_cast<float*>(act);  // [CW][gqa]
+    float* ll = mm + CW * MAX_GQA;              // [CW][gqa]
+    float* aa = ll + CW * MAX_GQA;              // [CW][gqa][D]
 #pragma unroll
     for (int h = 0; h < MAX_GQA; ++h) {
       if (h >= gqa) break;
       if (lane == 0) {
-        mm[warp * gqa + h] = s.m[h];
-        ll[warp * gqa + h] = s.l[h];
+        mm[warp * gqa + h] = m[h];
+        ll[warp * gqa + h] = lsum[h];
       }
+      if (grp == 0) {
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) aa[(warp * gqa + h) * D + lane * DPL + e] = s.acc[h][e];
+        for (int e = 0; e < 16; ++e) aa[(warp * gqa + h) * D + sub * 16 + e] = acc[h][e];
+      }
     }
     sync();
     for (int idx = tid; idx < gqa * D; idx += NC) {
@@ -388,6 +430,8 @@ struct Consumer {
   }
 
   // AttentionReduction (python_vm.py:360-401): exp2-weighted merge of partials.
+  // The partials' LSEs are staged in shared memory first so that every load of
+  // the merge is issued independently.
   __device__ void op_reduction(const Ins& ins) {
     const int l = ins.w[1], hs = ins.w[2], P = ins.w[3], terminal = ins.w[4], n = ins.w[5];
     const int out_slot = ins.w[6 + n];
@@ -397,23 +441,40 @@ struct Consumer {
     }
     stamp(1);
     const int D = p.D, gqa = p.gqa;
+    float* fac = reinterpret_cast<float*>(act);   // [gqa][n] exp2(lse - max)
+    float* den = fac + MAX_GQA * 32;              // [gqa]
+    for (int i = tid; i < gqa * n; i += NC)
+      fac[i] = __ldcg(p.lse + (size_t)(hs + i / n) * p.maxP + ins.w[6 + i % n]);
+    sync();
+    if (tid < gqa) {
+      float M = -INFINITY;
+      for (int j = 0; j < n; ++j) M = fmaxf(M, fac[tid * n + j]);
+      float s = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const float f = exp2f(fac[tid * n + j] - M);
+        fac[tid * n + j] = f;
+        s += f;
+      }
+      den[tid] = s;
+    }
+    sync();
     // compute first, write after a barrier: the output slot may be an input
-    float res[4], newlse[4];
+    float res[4];
     int cnt = 0;
     for (int idx = tid; idx < gqa * D; idx += NC, ++cnt) {
       const int h = idx / D, d = idx % D;
-      const size_t row = (size_t)(hs + h) * p.maxP;
-      float M = -INFINITY;
-      for (int j = 0; j < n; ++j) M = fmaxf(M, __ldcg(p.lse + row + ins.w[6 + j]));
-      float den = 0.f, num = 0.f;
-      for (int j = 0; j < n; ++j) {
-        const int slot = ins.w[6 + j];
-        const float f = exp2f(__ldcg(p.lse + row + slot) - M);
-        den += f;
-        num = fmaf(__ldcg(p.attn_o + (row + slot) * D + d), f, num);
+      const float* o = p.attn_o + (size_t)(hs + h) * p.maxP * D + d;
+      float num = 0.f;
+      for (int j0 = 0; j0 < n; j0 += 8) {
+        float vals[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          vals[j] = j0 + j < n ? __ldcg(o + (size_t)ins.w[6 + j0 + j] * D) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j0 + j < n) num = fmaf(vals[j], fac[h * n + j0 + j], num);
       }
-      res[cnt] = num / den;
-      newlse[cnt] = logf(den);
+      res[cnt] = num / den[h];
     }
     sync();
     cnt = 0;
@@ -424,7 +485,7 @@ struct Consumer {
       } else {
         const size_t row = (size_t)(hs + h) * p.maxP + out_slot;
         p.attn_o[row * D + d] = res[cnt];
-        if (d == 0) p.lse[row] = newlse[cnt];
+        if (d == 0) p.lse[row] = logf(den[h]);
       }
     }
     sync();
@@ -464,12 +525,12 @@ struct Consumer {
     }
     stamp(1);
     copy_to_act((o ? p.attn_out : p.silu) + (size_t)split * R, R);
+    stamp(3);
     // partial sums: [o_splits][H] for O_ProjResidual, then [down_splits][H]
     __nv_bfloat16* partials = p.split_partials + (size_t)(o ? 0 : p.o_splits) * p.H;
     for (int b = b0; b < b1; ++b) {
       float r0, r1;
       gemv_block(R, r0, r1);
-      if (broken) return;
       if (lane == 0) {
         const int row = b * 16 + 2 * warp;
         const float v0 = bf16r(r0), v1 = bf16r(r1);
@@ -525,12 +586,11 @@ struct Consumer {
     }
     stamp(1);
     rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H);
+    stamp(3);
     for (int j = 0; j < n; ++j) {
       float u0, u1, g0, g1;
       gemv_block(p.H, u0, u1);
-      if (broken) return;
       gemv_block(p.H, g0, g1);
-      if (broken) return;
       if (lane == 0) {
         const int row = ins.w[3 + j] * 16 + 2 * warp;
         const float gb0 = bf16r(g0), gb1 = bf16r(g1);
@@ -559,7 +619,6 @@ struct Consumer {
     for (int b = b0; b < b1; ++b) {
       float r0, r1;
       gemv_block(p.H, r0, r1);
-      if (broken) return;
       if (lane == 0)
         *reinterpret_cast<uint32_t*>(p.logits + b * 16 + 2 * warp) = pack_bf16x2(r0, r1);
     }
@@ -567,42 +626,61 @@ struct Consumer {
 };
 
 // ------------------------------------------------------------------ loader
+// Walks the queue's stage sequence a second time, ahead of the loads, issuing
+// L2 prefetches. Used only while the ring is full, so the prefetches fill HBM
+// idle time (consumers waiting on other SMs) instead of competing with loads.
+struct PrefetchCursor {
+  int i = 0, k = 0;
+  bool have = false;
+  long long g = 0;  // global stage index of (i, k)
+  Ins ins;
+  Plan pl;
+
+  // Issue the prefetch of the next stage; false when the queue is exhausted.
+  __device__ bool step(const KParams& p, int q, long long g_load) {
+    while (true) {
+      if (!have) {
+        if (i >= p.Q) return false;
+        fetch_ins(p, q, i, ins);
+        pl = make_plan(p, ins);
+        k = 0;
+        have = true;
+      }
+      if (k >= pl.ns) {
+        ++i;
+        have = false;
+        continue;
+      }
+      if (g >= g_load) do_stage<true>(p, ins, pl, k, nullptr, nullptr);
+      ++k;
+      ++g;
+      return true;
+    }
+  }
+};
+
 __device__ void run_loader(const KParams& p, Ring ring) {
   const int q = blockIdx.x;
-  Ins ins, pins;
-  Plan pl, ppl;
-  // prefetch cursor (L2 lookahead beyond the ring)
-  int pi = 0, pk = 0;
-  bool p_valid = false;
-  long long g_load = 0, g_pf = 0;
-  const bool pf_on = p.pf_stages > 0;
+  Ins ins;
+  PrefetchCursor pf;
+  long long g_load = 0;
+  const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
 
   for (int i = 0; i < p.Q; ++i) {
     fetch_ins(p, q, i, ins);
-    pl = make_plan(p, ins);
+    const Plan pl = make_plan(p, ins);
     for (int k = 0; k < pl.ns; ++k) {
-      if (pf_on) {
-        while (g_pf < g_load + p.pf_stages) {
-          if (!p_valid) {
-            if (pi >= p.Q) break;
-            fetch_ins(p, q, pi, pins);
-            ppl = make_plan(p, pins);
-            pk = 0;
-            p_valid = true;
-          }
-          if (pk >= ppl.ns) {
-            ++pi;
-            p_valid = false;
-            continue;
-          }
-          if (g_pf >= g_load) do_stage<true>(p, pins, ppl, pk, nullptr, nullptr);
-          ++pk;
-          ++g_pf;
+      uint64_t* empty = &ring.empty[ring.slot];
+      const uint32_t parity = ring.phase ^ 1u;
+      if (!mbar_try_wait(empty, parity)) {
+        // ring full: run the L2 prefetch ahead while waiting for a slot
+        bool more = p.pf_stages > 0;
+        while (more && pf.g < g_load + p.pf_stages && !mbar_try_wait(empty, parity))
+          more = pf.step(p, q, g_load);
+        if (!ring_wait(empty, parity, ring_timeout)) {
+          record_error(p, 4, i, pl.op, pl.layer, ring.slot, (int)ring.phase, -1);
+          return;
         }
-      }
-      if (!ring_wait(&ring.empty[ring.slot], ring.phase ^ 1u, 4 * p.timeout_ns + 2000000000ll)) {
-        record_error(p, 4, i, pl.op, pl.layer, ring.slot, (int)ring.phase, -1);
-        return;
       }
       do_stage<false>(p, ins, pl, k, ring.stages + (size_t)ring.slot * STAGE_BYTES,
                       &ring.full[ring.slot]);
@@ -661,7 +739,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   c.broken = false;
 
   Ins ins;
-  for (int i = 0; i < p.Q && !c.broken; ++i) {
+  for (int i = 0; i < p.Q; ++i) {
     c.iidx = i;
     fetch_ins(p, blockIdx.x, i, ins);
     const Plan pl = make_plan(p, ins);

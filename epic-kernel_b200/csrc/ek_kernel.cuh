@@ -45,7 +45,7 @@ constexpr int NUM_STAGES = 12;        // 192 KiB ring
 constexpr int CTRL_BYTES = 1024;      // mbarriers + reduction scratch
 constexpr int SMEM_BYTES = NUM_STAGES * STAGE_BYTES + ACT_BYTES + CTRL_BYTES;
 constexpr int GEMV_STAGE_COLS = 512;  // weight columns per stage (two 256-col boxes)
-constexpr int MAX_GQA = 8;
+constexpr int MAX_GQA = 4;  // query heads per KV head
 
 enum Op : int {
   OP_NOOP = 0,

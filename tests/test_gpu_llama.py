@@ -36,17 +36,23 @@ def golden(golden_dir):
     return np.load(golden_dir / "llama_tiny_step.npz")
 
 
-def assert_close_bf16(mine, ref, name, max_frac=0.02):
+def assert_close_bf16(mine, ref, name, max_frac=0.02, alt=None):
     """At most `max_frac` of the elements differ, and each difference is within
     two bf16 ulps of the element plus 2e-2 x std (cancellation in residual adds
-    can leave a tiny value with a large ulp distance)."""
+    can leave a tiny value with a large ulp distance). With `alt` (the
+    reordered-summation oracle), both bounds widen to twice alt's own
+    disagreement with `ref`."""
     mine = mine.detach().cpu().to(torch.bfloat16).reshape(-1)
     ref = ref.detach().cpu().to(torch.bfloat16).reshape(-1)
-    frac = (ulp_diff(mine, ref) > 0).float().mean().item()
-    assert frac <= max_frac, f"{name}: {frac:.3%} of elements differ"
     r = ref.float()
     ulp = torch.exp2(torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
     bound = 2 * ulp + 2e-2 * r.std()
+    if alt is not None:
+        alt = alt.detach().cpu().to(torch.bfloat16).reshape(-1)
+        max_frac = max(max_frac, 2 * (ulp_diff(alt, ref) > 0).float().mean().item())
+        bound = torch.maximum(bound, 2 * (alt.float() - r).abs().max())
+    frac = (ulp_diff(mine, ref) > 0).float().mean().item()
+    assert frac <= max_frac, f"{name}: {frac:.3%} of elements differ (allowed {max_frac:.3%})"
     excess = ((mine.float() - r).abs() - bound).max().item()
     assert excess <= 0, f"{name}: error exceeds bound by {excess}"
 
@@ -63,11 +69,15 @@ def test_tiny_step_vs_reference_interpreter(tiny_gpu, tiny_cpu, golden, pos):
     np.testing.assert_array_equal(g.barriers.cpu().numpy(), golden[f"p{pos}_barriers"])
     ref_logits = bf16_from_bits(golden[f"p{pos}_logits"])
     _, alt = noise_floor(tiny_cpu, pos, hidden)
-    assert_logits_within_floor(g.logits, ref_logits, alt.globs.logits)
+    a = alt.globs
+    assert_logits_within_floor(g.logits, ref_logits, a.logits)
     for name in ("post_ln_rope_q", "attn_out", "silu_out", "hidden_states"):
-        assert_close_bf16(getattr(g, name), bf16_from_bits(golden[f"p{pos}_{name}"]), name)
-    assert_close_bf16(g.k_cache[:, 0, pos], bf16_from_bits(golden[f"p{pos}_k_row"]), "k row")
-    assert_close_bf16(g.v_cache[:, 0, pos], bf16_from_bits(golden[f"p{pos}_v_row"]), "v row")
+        assert_close_bf16(getattr(g, name), bf16_from_bits(golden[f"p{pos}_{name}"]), name,
+                          alt=getattr(a, name))
+    assert_close_bf16(g.k_cache[:, 0, pos], bf16_from_bits(golden[f"p{pos}_k_row"]), "k row",
+                      alt=a.k_cache[:, 0, pos])
+    assert_close_bf16(g.v_cache[:, 0, pos], bf16_from_bits(golden[f"p{pos}_v_row"]), "v row",
+                      alt=a.v_cache[:, 0, pos])
     # rows past pos keep their poison (no stray writes)
     assert g.k_cache[:, 0, pos + 1 :].float().abs().max() > 50
 
