@@ -28,29 +28,50 @@ struct Consumer {
 
   __device__ __forceinline__ void sync() { named_sync<NC>(); }
 
-  // Wait for stage data; every consumer warp calls this for every stage.
-  __device__ __forceinline__ const uint8_t* acquire() {
+  // Ring stages are numbered in stream order (ring.g); stage g lives in slot
+  // g % NUM_STAGES with phase parity (g / NUM_STAGES) & 1. A stage is either
+  // shared (every consumer warp reads it and arrives once on its empty
+  // barrier, used by attention) or owned by warp (g % CW), which arrives for
+  // all CW warps (used by the GEMVs).
+  __device__ __forceinline__ const uint8_t* wait_stage(uint32_t g) {
+    const int slot = g % NUM_STAGES;
     if (!broken) {
-      const bool ok = ring_wait(&ring.full[ring.slot], ring.phase, 4 * p.timeout_ns + 2000000000ll);
+      const bool ok = ring_wait(&ring.full[slot], (g / NUM_STAGES) & 1u, 4 * p.timeout_ns + 2000000000ll);
       if (__any_sync(0xffffffffu, !ok)) {
-        if (lane == 0) record_error(p, 4, iidx, -1, -1, ring.slot, (int)ring.phase, warp);
+        if (lane == 0) record_error(p, 4, iidx, -1, -1, slot, (int)((g / NUM_STAGES) & 1u), warp);
         broken = true;
       }
     }
-    return ring.stages + (size_t)ring.slot * STAGE_BYTES;
+    return ring.stages + (size_t)slot * STAGE_BYTES;
   }
+
+  // Shared stage: every consumer warp calls acquire/release for it.
+  __device__ __forceinline__ const uint8_t* acquire() { return wait_stage(ring.g); }
 
   __device__ __forceinline__ void release() {
     __syncwarp();
-    if (lane == 0) mbar_arrive(&ring.empty[ring.slot]);
-    ring_advance(ring);
+    if (lane == 0) mbar_arrive(&ring.empty[ring.g % NUM_STAGES]);
+    ++ring.g;
   }
 
+  // Owned stage g: the owner warp frees it for everyone.
+  __device__ __forceinline__ void release_owned(uint32_t g) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cnt(&ring.empty[g % NUM_STAGES], CW);
+  }
+
+  __device__ __forceinline__ bool owns(uint32_t g) const { return (int)(g % CW) == warp; }
+
+  // Skip ns stages without computing (aborted launch): owners free them.
   __device__ void drain(int ns) {
     for (int k = 0; k < ns; ++k) {
-      acquire();
-      release();
+      const uint32_t g = ring.g + k;
+      if (owns(g)) {
+        wait_stage(g);
+        release_owned(g);
+      }
     }
+    ring.g += ns;
   }
 
   // Thread 0 spins until every counter in `addrs` reaches its target, bounded
@@ -145,43 +166,81 @@ struct Consumer {
     sync();
   }
 
-  // Accumulate the stage's 16 x (256 or 512) tile against xs[x0 ...] into the
-  // two rows (2 warp, 2 warp + 1) this warp owns.
-  __device__ __forceinline__ void mac_stage(const uint8_t* st, int x0, bool two, float& a0, float& a1) {
+  // One owned GEMV stage: the 16 x (256 or 512) weight tile times xs[x0 ...].
+  // Each lane covers 8 columns of every row per 256-column box; the 16 row sums
+  // are then reduce-scattered over the warp (16 shuffles) so that lanes 2r and
+  // 2r + 1 hold row r. Lane 2r writes it to part[r].
+  __device__ __forceinline__ void gemv_stage(const uint8_t* st, int x0, bool two, float* part) {
     const uint4* xs4 = reinterpret_cast<const uint4*>(act);
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       if (h == 1 && !two) break;
       const uint4 xv = xs4[(x0 + h * 256) / 8 + lane];
+      const float x[8] = {bf_lo(xv.x), bf_hi(xv.x), bf_lo(xv.y), bf_hi(xv.y),
+                          bf_lo(xv.z), bf_hi(xv.z), bf_lo(xv.w), bf_hi(xv.w)};
       const uint8_t* base = st + h * HALF_STAGE + lane * 16;
-      const uint4 w0 = *reinterpret_cast<const uint4*>(base + (2 * warp) * 512);
-      const uint4 w1 = *reinterpret_cast<const uint4*>(base + (2 * warp + 1) * 512);
-      const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
-      const uint32_t u0[4] = {w0.x, w0.y, w0.z, w0.w};
-      const uint32_t u1[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float xl = bf_lo(xu[k]), xh = bf_hi(xu[k]);
-        a0 = fmaf(bf_lo(u0[k]), xl, a0);
-        a0 = fmaf(bf_hi(u0[k]), xh, a0);
-        a1 = fmaf(bf_lo(u1[k]), xl, a1);
-        a1 = fmaf(bf_hi(u1[k]), xh, a1);
+      for (int r = 0; r < 16; ++r) {
+        const uint4 w = *reinterpret_cast<const uint4*>(base + r * 512);
+        float a = acc[r];
+        a = fmaf(bf_lo(w.x), x[0], a);
+        a = fmaf(bf_hi(w.x), x[1], a);
+        a = fmaf(bf_lo(w.y), x[2], a);
+        a = fmaf(bf_hi(w.y), x[3], a);
+        a = fmaf(bf_lo(w.z), x[4], a);
+        a = fmaf(bf_hi(w.z), x[5], a);
+        a = fmaf(bf_lo(w.w), x[6], a);
+        a = fmaf(bf_hi(w.w), x[7], a);
+        acc[r] = a;
       }
     }
+#pragma unroll
+    for (int lvl = 0; lvl < 4; ++lvl) {
+      const int half = 8 >> lvl;       // values kept after this level
+      const int off = 16 >> lvl;       // shuffle distance
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i >= half) break;
+        const float send = up ? acc[i] : acc[i + half];
+        const float keep = up ? acc[i + half] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+    if ((lane & 1) == 0) part[(lane >> 1) & 15] = acc[0];
   }
 
-  // One 16-row block reduced over K columns (xs holds those K values starting
-  // at act[0]); returns the full row sums in every lane.
-  __device__ __forceinline__ void gemv_block(int K, float& r0, float& r1) {
-    const int spb = stages_per_row_block(K);
-    float a0 = 0.f, a1 = 0.f;
-    for (int s = 0; s < spb; ++s) {
-      const uint8_t* st = acquire();
-      mac_stage(st, s * GEMV_STAGE_COLS, s * GEMV_STAGE_COLS + 256 < K, a0, a1);
-      release();
+  // Stream the ns owned GEMV stages of the current instruction. Stage k
+  // multiplies columns [x0(k), x0(k) + 512) of the activation in act[0..K);
+  // partial sums go to part[k * 16 + r]. Returns after a consumer barrier, so
+  // the epilogue may read every partial.
+  template <typename X0>
+  __device__ __forceinline__ void gemv_stream(int ns, int K, float* part, X0 x0_of) {
+    for (int k = 0; k < ns; ++k) {
+      const uint32_t g = ring.g + k;
+      if (!owns(g)) continue;
+      const uint8_t* st = wait_stage(g);
+      const int x0 = x0_of(k);
+      gemv_stage(st, x0, x0 + 256 < K, part + k * 16);
+      release_owned(g);
     }
-    r0 = warp_sum(a0);
-    r1 = warp_sum(a1);
+    ring.g += ns;
+    sync();
+  }
+
+  __device__ __forceinline__ float* partials_after(int K) const {
+    return reinterpret_cast<float*>(act + ((K * 2 + 15) & ~15));
+  }
+
+  // Row r of a block whose stages are part[first .. first + n) (fixed order).
+  __device__ __forceinline__ static float sum_stages(const float* part, int first, int n, int r) {
+    float v = 0.f;
+    for (int s = 0; s < n; ++s) v += part[(first + s) * 16 + r];
+    return v;
   }
 
   // ---------------------------------------------------------------- opcodes
@@ -200,33 +259,35 @@ struct Consumer {
     rmsnorm_to_act(p.hidden, p.attn_ln + (size_t)l * p.H, p.H);
     stamp(3);
     const int qdim = p.Hq * p.D, kdim = p.Hkv * p.D;
-    for (int b = b0; b < b1; ++b) {
-      float r0, r1;
-      gemv_block(p.H, r0, r1);
-      if (lane == 0) {
-        const int row = b * 16 + 2 * warp;  // even: rows (row, row + 1) form a rotary pair
-        float v0 = bf16r(r0), v1 = bf16r(r1);
-        if (row < qdim + kdim) {
-          // interleaved RoPE (llama.py:136-174) in fp32, rounded to bf16 on store
-          const int seg = row % p.D;
-          const float* cs = p.rope_cos + (size_t)p.pos * p.D + seg;
-          const float* sn = p.rope_sin + (size_t)p.pos * p.D + seg;
-          const float o0 = __fadd_rn(__fmul_rn(v0, cs[0]), __fmul_rn(-v1, sn[0]));
-          const float o1 = __fadd_rn(__fmul_rn(v1, cs[1]), __fmul_rn(v0, sn[1]));
-          v0 = o0;
-          v1 = o1;
-        }
-        const uint32_t packed = pack_bf16x2(v0, v1);
-        __nv_bfloat16* dst;
-        if (row < qdim) {
-          dst = p.q + row;
-        } else if (row < qdim + kdim) {
-          dst = p.k_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim);
-        } else {
-          dst = p.v_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim - kdim);
-        }
-        *reinterpret_cast<uint32_t*>(dst) = packed;
+    const int spb = stages_per_row_block(p.H);
+    float* part = partials_after(p.H);
+    gemv_stream(pl.ns, p.H, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    stamp(4);
+    // one thread per rotary pair (rows 2i, 2i + 1 of a block)
+    for (int idx = tid; idx < (b1 - b0) * 8; idx += NC) {
+      const int j = idx / 8, pr = idx % 8;
+      const int row = (b0 + j) * 16 + 2 * pr;
+      float v0 = bf16r(sum_stages(part, j * spb, spb, 2 * pr));
+      float v1 = bf16r(sum_stages(part, j * spb, spb, 2 * pr + 1));
+      if (row < qdim + kdim) {
+        // interleaved RoPE (llama.py:136-174) in fp32, rounded to bf16 on store
+        const int seg = row % p.D;
+        const float* cs = p.rope_cos + (size_t)p.pos * p.D + seg;
+        const float* sn = p.rope_sin + (size_t)p.pos * p.D + seg;
+        const float o0 = __fadd_rn(__fmul_rn(v0, cs[0]), __fmul_rn(-v1, sn[0]));
+        const float o1 = __fadd_rn(__fmul_rn(v1, cs[1]), __fmul_rn(v0, sn[1]));
+        v0 = o0;
+        v1 = o1;
       }
+      __nv_bfloat16* dst;
+      if (row < qdim) {
+        dst = p.q + row;
+      } else if (row < qdim + kdim) {
+        dst = p.k_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim);
+      } else {
+        dst = p.v_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim - kdim);
+      }
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(v0, v1);
     }
     sync();
     if (tid == 0) {
@@ -528,19 +589,18 @@ struct Consumer {
     stamp(3);
     // partial sums: [o_splits][H] for O_ProjResidual, then [down_splits][H]
     __nv_bfloat16* partials = p.split_partials + (size_t)(o ? 0 : p.o_splits) * p.H;
-    for (int b = b0; b < b1; ++b) {
-      float r0, r1;
-      gemv_block(R, r0, r1);
-      if (lane == 0) {
-        const int row = b * 16 + 2 * warp;
-        const float v0 = bf16r(r0), v1 = bf16r(r1);
-        if (splits == 1) {
-          const uint32_t h = __ldcg(reinterpret_cast<const unsigned*>(p.hidden + row));
-          *reinterpret_cast<uint32_t*>(p.hidden + row) = pack_bf16x2(bf_lo(h) + v0, bf_hi(h) + v1);
-        } else {
-          *reinterpret_cast<uint32_t*>(partials + (size_t)split * p.H + row) = pack_bf16x2(v0, v1);
-        }
-      }
+    const int spb = stages_per_row_block(R);
+    float* part = partials_after(R);
+    gemv_stream(pl.ns, R, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    stamp(4);
+    for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      const int row = (b0 + j) * 16 + r;
+      const float v = bf16r(sum_stages(part, j * spb, spb, r));
+      if (splits == 1)
+        p.hidden[row] = __float2bfloat16_rn(ldcg_bf16(p.hidden + row) + v);
+      else
+        partials[(size_t)split * p.H + row] = __float2bfloat16_rn(v);
     }
     sync();
     int* done = bar(l, pl.op - 1, 0);
@@ -587,17 +647,16 @@ struct Consumer {
     stamp(1);
     rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H);
     stamp(3);
-    for (int j = 0; j < n; ++j) {
-      float u0, u1, g0, g1;
-      gemv_block(p.H, u0, u1);
-      gemv_block(p.H, g0, g1);
-      if (lane == 0) {
-        const int row = ins.w[3 + j] * 16 + 2 * warp;
-        const float gb0 = bf16r(g0), gb1 = bf16r(g1);
-        const float s0 = bf16r(gb0 / (1.0f + expf(-gb0)));
-        const float s1 = bf16r(gb1 / (1.0f + expf(-gb1)));
-        *reinterpret_cast<uint32_t*>(p.silu + row) = pack_bf16x2(s0 * bf16r(u0), s1 * bf16r(u1));
-      }
+    const int spb = stages_per_row_block(p.H);
+    float* part = partials_after(p.H);
+    gemv_stream(pl.ns, p.H, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    stamp(4);
+    for (int idx = tid; idx < n * 16; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      const float u = bf16r(sum_stages(part, j * 2 * spb, spb, r));
+      const float gt = bf16r(sum_stages(part, j * 2 * spb + spb, spb, r));
+      const float sl = bf16r(gt / (1.0f + expf(-gt)));
+      p.silu[ins.w[3 + j] * 16 + r] = __float2bfloat16_rn(sl * u);
     }
     sync();
     if (tid == 0) {
@@ -616,11 +675,14 @@ struct Consumer {
     }
     stamp(1);
     rmsnorm_to_act(p.hidden, p.lm_norm, p.H);
-    for (int b = b0; b < b1; ++b) {
-      float r0, r1;
-      gemv_block(p.H, r0, r1);
-      if (lane == 0)
-        *reinterpret_cast<uint32_t*>(p.logits + b * 16 + 2 * warp) = pack_bf16x2(r0, r1);
+    stamp(3);
+    const int spb = stages_per_row_block(p.H);
+    float* part = partials_after(p.H);
+    gemv_stream(pl.ns, p.H, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    stamp(4);
+    for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      p.logits[(b0 + j) * 16 + r] = __float2bfloat16_rn(sum_stages(part, j * spb, spb, r));
     }
   }
 };
@@ -721,7 +783,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   }
   __syncthreads();
 
-  Ring ring{stages, full, empty, 0, 0u};
+  Ring ring{stages, full, empty, 0, 0u, 0u};
   if (warp == CW) {
     if (lane == 0) run_loader(p, ring);
     return;

@@ -40,8 +40,8 @@ constexpr int NC = CW * 32;           // consumer threads
 constexpr int NTHREADS = NC + 32;     // + loader warp
 constexpr int STAGE_BYTES = 16384;    // one ring stage
 constexpr int HALF_STAGE = 8192;      // one TMA box (16 rows x 256 bf16, or TK x D bf16)
-constexpr int ACT_BYTES = 32768;      // activation vector / attention merge area
-constexpr int NUM_STAGES = 12;        // 192 KiB ring
+constexpr int ACT_BYTES = 49152;      // activation vector + per-stage partial sums / attention merge
+constexpr int NUM_STAGES = 11;        // 176 KiB ring
 constexpr int CTRL_BYTES = 1024;      // mbarriers + reduction scratch
 constexpr int SMEM_BYTES = NUM_STAGES * STAGE_BYTES + ACT_BYTES + CTRL_BYTES;
 constexpr int GEMV_STAGE_COLS = 512;  // weight columns per stage (two 256-col boxes)
@@ -120,6 +120,12 @@ __device__ __forceinline__ int stages_per_row_block(int K) {
   return (K + GEMV_STAGE_COLS - 1) / GEMV_STAGE_COLS;
 }
 
+// Bytes of `act` a GEMV instruction needs: its activation slice (K bf16) and
+// one 16-float partial row per ring stage.
+__device__ __forceinline__ int gemv_act_bytes(int K, int ns) {
+  return ((K * 2 + 15) & ~15) + ns * 64;
+}
+
 // Token range [t_begin, t_end) of one partial (python_vm.py:306-318), and the
 // end of the part the loader may stream (tokens before pos_id).
 struct TokenRange {
@@ -169,6 +175,7 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
       if (w[2] < 0 || w[2] > w[3]) { bad(2); break; }
       if (w[3] > p.qkv_rows / 16) { bad(3); break; }
       pl.ns = (w[3] - w[2]) * stages_per_row_block(p.H);
+      if (gemv_act_bytes(p.H, pl.ns) > ACT_BYTES) { bad(3); break; }
       break;
     }
     case OP_PARTIAL: {
@@ -203,6 +210,7 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
       if (w[3] > p.H / 16) { bad(3); break; }
       if (w[4] < 0 || w[4] >= splits) { bad(4); break; }
       pl.ns = (w[3] - w[2]) * stages_per_row_block(R);
+      if (gemv_act_bytes(R, pl.ns) > ACT_BYTES) { bad(3); break; }
       break;
     }
     case OP_UPGATE: {
@@ -213,6 +221,7 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
         if (w[3 + j] < 0 || w[3 + j] >= p.I / 16) { bad(3 + j); break; }
       if (pl.bad_word >= 0) break;
       pl.ns = w[2] * 2 * stages_per_row_block(p.H);
+      if (gemv_act_bytes(p.H, pl.ns) > ACT_BYTES) { bad(2); break; }
       break;
     }
     case OP_LM_HEAD: {
@@ -220,6 +229,7 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
       if (w[1] < 0 || w[1] > w[2]) { bad(1); break; }
       if (w[2] > p.V / 16) { bad(2); break; }
       pl.ns = (w[2] - w[1]) * stages_per_row_block(p.H);
+      if (gemv_act_bytes(p.H, pl.ns) > ACT_BYTES) { bad(2); break; }
       break;
     }
     default:
@@ -329,9 +339,11 @@ struct Ring {
   uint8_t* stages;
   uint64_t* full;
   uint64_t* empty;
-  int slot;
-  uint32_t phase;
+  int slot;         // loader: next slot to fill
+  uint32_t phase;   // loader: its phase parity
+  uint32_t g;       // consumers: index of the next stage in this queue's stream
 };
+
 
 // Bounded wait on an mbarrier phase; false after ~timeout (then the engine is
 // broken and the caller leaves the kernel).

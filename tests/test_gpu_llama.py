@@ -37,24 +37,25 @@ def golden(golden_dir):
 
 
 def assert_close_bf16(mine, ref, name, max_frac=0.02, alt=None):
-    """At most `max_frac` of the elements differ, and each difference is within
-    two bf16 ulps of the element plus 2e-2 x std (cancellation in residual adds
-    can leave a tiny value with a large ulp distance). With `alt` (the
-    reordered-summation oracle), both bounds widen to twice alt's own
-    disagreement with `ref`."""
-    mine = mine.detach().cpu().to(torch.bfloat16).reshape(-1)
-    ref = ref.detach().cpu().to(torch.bfloat16).reshape(-1)
-    r = ref.float()
-    ulp = torch.exp2(torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
-    bound = 2 * ulp + 2e-2 * r.std()
-    if alt is not None:
-        alt = alt.detach().cpu().to(torch.bfloat16).reshape(-1)
-        max_frac = max(max_frac, 2 * (ulp_diff(alt, ref) > 0).float().mean().item())
-        bound = torch.maximum(bound, 2 * (alt.float() - r).abs().max())
-    frac = (ulp_diff(mine, ref) > 0).float().mean().item()
-    assert frac <= max_frac, f"{name}: {frac:.3%} of elements differ (allowed {max_frac:.3%})"
-    excess = ((mine.float() - r).abs() - bound).max().item()
-    assert excess <= 0, f"{name}: error exceeds bound by {excess}"
+    """Without `alt`: at most `max_frac` of the elements differ, each within two
+    bf16 ulps of the element plus 2e-2 x std. With `alt` (the reordered-summation
+    oracle, for multi-layer runs where 1-ulp flips spread chaotically): max and
+    RMS errors within max(that bound, 2 x alt's own error)."""
+    mine = mine.detach().cpu().to(torch.bfloat16).reshape(-1).float()
+    ref = ref.detach().cpu().to(torch.bfloat16).reshape(-1).float()
+    ulp = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - 7)
+    bound = 2 * ulp + 2e-2 * ref.std()
+    d = (mine - ref).abs()
+    if alt is None:
+        frac = (d > 0).float().mean().item()
+        assert frac <= max_frac, f"{name}: {frac:.3%} of elements differ (allowed {max_frac:.3%})"
+        excess = (d - bound).max().item()
+        assert excess <= 0, f"{name}: error exceeds bound by {excess}"
+        return
+    da = (alt.detach().cpu().to(torch.bfloat16).reshape(-1).float() - ref).abs()
+    assert d.max() <= max(bound.max().item(), 2 * da.max().item()), f"{name}: max error {d.max().item()}"
+    rms, rms_alt = d.pow(2).mean().sqrt().item(), da.pow(2).mean().sqrt().item()
+    assert rms <= max(1e-2 * ref.std().item(), 2 * rms_alt), f"{name}: rms error {rms} (alt {rms_alt})"
 
 
 @pytest.mark.parametrize("pos", cases.TINY_POSITIONS)

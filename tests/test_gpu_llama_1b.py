@@ -42,34 +42,65 @@ def test_1b_step_kv2048_vs_oracle():
     assert int(s.globs.logits.argmax()) == int(ref.globs.logits.argmax())
 
 
+# The reference interpreter re-run with another (equally valid) fp32 summation
+# order disagrees with itself by up to 0.117 in the Llama-1B logits, and its
+# free-running greedy stream leaves the reference's at generated token 20,
+# where the reference's top-2 margin is 0.078. Steps whose reference margin is
+# below this bound are therefore not decidable by any implementation that does
+# not replicate the CPU's summation order.
+NEAR_TIE = 0.125
+
+
+def _decode(gen, model, prompt, forced, total):
+    """Run `total` decode steps. The input at position pos is the prompt token,
+    else forced[pos - len(prompt) + 1] if given, else our previous output."""
+    outs = []
+    cur = int(prompt[0])
+    for pos in range(total):
+        out = int(gen.run(torch.tensor([[cur]], device="cuda"), pos))
+        outs.append(out)
+        if pos + 1 < len(prompt):
+            cur = int(prompt[pos + 1])
+        elif forced is not None:
+            cur = int(forced[pos + 1 - len(prompt)])
+        else:
+            cur = out
+    return outs
+
+
 def test_1b_greedy_tokens_match_reference(golden_dir):
     path = golden_dir / "llama1b_decode192.npz"
     if not path.exists():
         pytest.skip("llama1b_decode192.npz not generated")
     gold = np.load(path)
-    prompt = torch.from_numpy(gold["prompt"])
+    prompt = gold["prompt"]
     expected = gold["greedy_tokens"]
     margins = gold["top2_margin"]
-    prompt_len, ntok = len(prompt), len(expected)
+    P, N = len(prompt), len(expected)
     model = LlamaForCausalLM.random_init(
         llama_3_2_1b_config(), ExtraModelConfig(interleave_rope=True, max_len_override=256),
         seed=0, device="cuda")
-    sched = LatencyScheduleBuilder.build(model, seq_len=prompt_len + ntok)
+    sched = LatencyScheduleBuilder.build(model, seq_len=P + N)
     tensorize_instructions(sched.globs, assign_to_sms("rr", schedule=sched))
     gen = MK_Generator(model, LatencyMK_Interpreter(), sched)
-    toks = []
-    cur = int(prompt[0])
-    for pos in range(prompt_len + ntok - 1):
-        out = gen.run(torch.tensor([[cur]], device="cuda"), pos)
-        if pos + 1 < prompt_len:
-            cur = int(prompt[pos + 1])
-        else:
-            cur = int(out)
-            toks.append(cur)
     import mk_llama
 
+    # teacher-forced: the reference's own tokens are fed back; every decidable
+    # step must produce the reference's token
+    outs = _decode(gen, model, prompt, expected, P + N - 1)
     mk_llama.check()
-    mism = [i for i, (a, b) in enumerate(zip(toks, expected)) if a != b]
-    first = mism[0] if mism else None
-    assert not mism, (f"greedy tokens differ first at step {first}: {toks[first]} vs {expected[first]} "
-                      f"(reference top-2 margin there {margins[prompt_len - 1 + first]:.4f})")
+    gen_margins = margins[P - 1 :]
+    ours = outs[P - 1 :]
+    wrong = [i for i in range(N) if ours[i] != expected[i] and gen_margins[i] >= NEAR_TIE]
+    assert not wrong, f"teacher-forced step {wrong[0]}: {ours[wrong[0]]} vs {expected[wrong[0]]}"
+    decidable = int((gen_margins >= NEAR_TIE).sum())
+    assert decidable >= N // 2
+
+    # free-running: identical tokens up to the first near-tie of the reference
+    model.stacked_kv_cache[0].zero_()
+    model.stacked_kv_cache[1].zero_()
+    free = _decode(gen, model, prompt, None, P + N - 1)[P - 1 :]
+    ties = [i for i in range(N) if gen_margins[i] < NEAR_TIE]
+    prefix = ties[0] if ties else N
+    assert free[:prefix] == list(expected[:prefix]), (
+        f"free-running tokens differ before the first near-tie (step {prefix})")
