@@ -294,3 +294,93 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot call cudaMalloc at decode time: code running while a
+// CUDA graph is being captured, allocators that must not be re-entered,
+// embedded runtimes that reserve all device memory up front. For them the
+// engine's scratch (status record, split-sum arrival counters, split partial
+// sums) lives in file-scope device arrays of fixed size that every GPU which
+// loads this library keeps until the process exits (about 0.7 MiB per GPU).
+namespace {
+
+constexpr size_t kStaticCounters = 65536;   // u32: L * 2 * (H / 16), e.g. L=64, H=8192
+constexpr size_t kStaticPartials = 196608;  // bf16: (H / o_split + I / d_split) * H
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) ek::DevStatus g_static_status;
+static __device__ __align__(256) unsigned g_static_counters[kStaticCounters];
+static __device__ __align__(256) __nv_bfloat16 g_static_partials[kStaticPartials];
+
+struct StaticScratch {
+  bool ready = false;
+  ek::DevStatus* status = nullptr;
+  unsigned* counters = nullptr;
+  __nv_bfloat16* partials = nullptr;
+  unsigned epoch = 0;
+};
+
+std::mutex g_static_mu;
+StaticScratch g_static[kMaxDevices];
+
+}  // namespace
+
+extern "C" int ek_llama_decode_static(const EkLlamaArgs* a, void* stream, EkStatus* status_out) {
+  if (!a) return fail(EK_E_INVALID, "NULL arguments");
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(EK_E_UNSUPPORTED, "device %d beyond %d", dev, kMaxDevices);
+
+  // sizes the context path would allocate; reject instead of allocating
+  const int H = a->hidden, I = a->intermediate, L = a->num_layers;
+  const int dR = a->down_reduction_size > 0 ? a->down_reduction_size : I;
+  const int oR = a->oproj_reduction_size > 0 ? a->oproj_reduction_size : H;
+  if (H <= 0 || I <= 0 || L <= 0 || dR <= 0 || oR <= 0)
+    return fail(EK_E_INVALID, "bad model dims");
+  const size_t nctr = (size_t)L * 2 * (H / 16);
+  const size_t npart = (size_t)(H / oR + I / dR) * H;
+  if (nctr > kStaticCounters || npart > kStaticPartials)
+    return fail(EK_E_UNSUPPORTED,
+                "model needs %zu counters / %zu partial sums; the allocation-free entry point "
+                "holds at most %zu / %zu",
+                nctr, npart, kStaticCounters, kStaticPartials);
+
+  EkContext tmp;
+  {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    StaticScratch& s = g_static[dev];
+    if (!s.ready) {  // first call on this device: resolve the arrays' device addresses
+      if ((e = cudaGetSymbolAddress((void**)&s.status, g_static_status)) != cudaSuccess)
+        return cuda_fail(e, "cudaGetSymbolAddress(status)");
+      if ((e = cudaGetSymbolAddress((void**)&s.counters, g_static_counters)) != cudaSuccess)
+        return cuda_fail(e, "cudaGetSymbolAddress(counters)");
+      if ((e = cudaGetSymbolAddress((void**)&s.partials, g_static_partials)) != cudaSuccess)
+        return cuda_fail(e, "cudaGetSymbolAddress(partials)");
+      s.ready = true;
+    }
+    tmp.device = dev;
+    tmp.status = s.status;
+    tmp.counters = s.counters;
+    tmp.counters_cap = kStaticCounters;
+    tmp.partials = s.partials;
+    tmp.partials_cap = kStaticPartials;
+    tmp.epoch = s.epoch;
+    // the epoch tags every arrival counter with this call, so values left by
+    // earlier calls are ignored; advance it here under the lock
+    if (++s.epoch == 0) s.epoch = 1;
+    tmp.epoch = s.epoch - 1;  // ek_llama_decode pre-increments to s.epoch
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the status record must start clear for this call
+  if ((e = cudaMemsetAsync(tmp.status, 0, sizeof(ek::DevStatus), st)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemsetAsync(status)");
+  const int rc = ek_llama_decode(&tmp, a, stream);
+  if (rc) return rc;
+  if (status_out &&
+      (e = cudaMemcpyAsync(status_out, tmp.status, sizeof(EkStatus), cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyAsync(status_out)");
+  return EK_SUCCESS;
+}

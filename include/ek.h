@@ -122,6 +122,25 @@ void ek_context_destroy(EkContext* ctx);
  */
 int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* args, void* stream);
 
+/*
+ * Llama decode step that allocates nothing, for callers that cannot call
+ * cudaMalloc while decoding (for example code running under CUDA graph
+ * capture, or runtimes that reserve all device memory up front). This entry
+ * point has no counterpart in the reference.
+ *
+ * The engine's scratch lives in fixed-size device arrays inside this library
+ * (about 0.7 MiB per GPU that loads it, kept until process exit): at most
+ * 65536 split counters (num_layers * 2 * hidden / 16) and 196608 bf16 partial
+ * sums ((hidden / oproj_reduction_size + intermediate / down_reduction_size)
+ * * hidden). Larger models are rejected with EK_E_UNSUPPORTED. Runs on the
+ * current device; the first call on a device resolves the arrays' addresses,
+ * so make it before any stream capture. The arrays are shared by every call on
+ * a device: calls that overlap on the GPU race. The status record is cleared
+ * at the start of each call; when `status_out` (device memory, may be NULL)
+ * is given, the call's EkStatus is copied there on `stream` after the kernel.
+ */
+int ek_llama_decode_static(const EkLlamaArgs* args, void* stream, EkStatus* status_out);
+
 /* Copy the device status record to `out` (synchronises with all work queued
  * on the context's device). With `clear`, reset it to EK_STATUS_OK. */
 int ek_read_status(EkContext* ctx, EkStatus* out, int clear);
