@@ -245,15 +245,20 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   std::memset(&p, 0, sizeof(p));
   const int qkv_rows = (Hq + 2 * Hkv) * D;
   const int tk = ek::HALF_STAGE / (D * 2);
-  if ((rc = encode_matrix(&p.tm_qkv, a->qkv_weights, (long long)L * qkv_rows, H, "qkv_weights"))) return rc;
-  if ((rc = encode_matrix(&p.tm_o, a->o_weights, (long long)L * H, H, "o_weights"))) return rc;
-  if ((rc = encode_matrix(&p.tm_up, a->up_weights, (long long)L * I, H, "up_weights"))) return rc;
-  if ((rc = encode_matrix(&p.tm_gate, a->gate_weights, (long long)L * I, H, "gate_weights"))) return rc;
-  if ((rc = encode_matrix(&p.tm_down, a->down_weights, (long long)L * H, I, "down_weights"))) return rc;
-  if ((rc = encode_matrix(&p.tm_lm, a->lm_head_weights, V, H, "lm_head_weights"))) return rc;
   if ((rc = encode_kv(&p.tm_k, a->k_cache, (long long)L * a->kv_len, Hkv, D, tk, "k_cache"))) return rc;
   if ((rc = encode_kv(&p.tm_v, a->v_cache, (long long)L * a->kv_len, Hkv, D, tk, "v_cache"))) return rc;
 
+  p.w_qkv = static_cast<const __nv_bfloat16*>(a->qkv_weights);
+  p.w_o = static_cast<const __nv_bfloat16*>(a->o_weights);
+  p.w_up = static_cast<const __nv_bfloat16*>(a->up_weights);
+  p.w_gate = static_cast<const __nv_bfloat16*>(a->gate_weights);
+  p.w_down = static_cast<const __nv_bfloat16*>(a->down_weights);
+  p.w_lm = static_cast<const __nv_bfloat16*>(a->lm_head_weights);
+  p.rows_qkv = (long long)L * qkv_rows;
+  p.rows_o = (long long)L * H;
+  p.rows_up = (long long)L * I;
+  p.rows_down = (long long)L * H;
+  p.rows_lm = V;
   p.barriers = a->barriers;
   p.instructions = a->instructions;
   p.timings = a->timings;

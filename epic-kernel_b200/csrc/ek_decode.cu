@@ -74,6 +74,11 @@ struct Consumer {
     ring.g += ns;
   }
 
+  // Publication rule: every consumer thread writes its results, the consumer
+  // warps pass a named barrier, then thread 0 bumps the counter with
+  // red.release.gpu. Release is cumulative over the barrier, so readers that
+  // acquire the counter see all those writes (they read with ld.global.cg).
+  //
   // Thread 0 spins until every counter in `addrs` reaches its target, bounded
   // by p.timeout_ns. Returns (to all consumer threads) whether to run the op.
   __device__ bool wait_counters(int n, int* const* addrs, const int* targets, int opcode, int layer) {
@@ -166,25 +171,26 @@ struct Consumer {
     sync();
   }
 
-  // One owned GEMV stage: the 16 x (256 or 512) weight tile times xs[x0 ...].
-  // Each lane covers 8 columns of every row per 256-column box; the 16 row sums
-  // are then reduce-scattered over the warp (16 shuffles) so that lanes 2r and
-  // 2r + 1 hold row r. Lane 2r writes it to part[r].
-  __device__ __forceinline__ void gemv_stage(const uint8_t* st, int x0, bool two, float* part) {
-    const uint4* xs4 = reinterpret_cast<const uint4*>(act);
-    float acc[16];
+  // One owned GEMV stage: RPS row segments of `len` columns (row i at
+  // st + i * len * 2) times act[xcol0 .. xcol0 + len). Lanes stride over 16-byte
+  // pieces, so every shared-memory load is conflict-free and each activation
+  // piece serves all RPS rows. The RPS row sums are then reduce-scattered over
+  // the warp and written to part[0 .. RPS).
+  template <int RPS>
+  __device__ __forceinline__ void gemv_rows(const uint8_t* st, int xcol0, int len, float* part) {
+    const uint4* xs4 = reinterpret_cast<const uint4*>(act) + xcol0 / 8;
+    float acc[RPS];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      if (h == 1 && !two) break;
-      const uint4 xv = xs4[(x0 + h * 256) / 8 + lane];
+    for (int r = 0; r < RPS; ++r) acc[r] = 0.f;
+    const int pieces = len / 8;
+#pragma unroll 2
+    for (int pc = lane; pc < pieces; pc += 32) {
+      const uint4 xv = xs4[pc];
       const float x[8] = {bf_lo(xv.x), bf_hi(xv.x), bf_lo(xv.y), bf_hi(xv.y),
                           bf_lo(xv.z), bf_hi(xv.z), bf_lo(xv.w), bf_hi(xv.w)};
-      const uint8_t* base = st + h * HALF_STAGE + lane * 16;
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        const uint4 w = *reinterpret_cast<const uint4*>(base + r * 512);
+      for (int r = 0; r < RPS; ++r) {
+        const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)r * len * 2 + pc * 16);
         float a = acc[r];
         a = fmaf(bf_lo(w.x), x[0], a);
         a = fmaf(bf_hi(w.x), x[1], a);
@@ -197,36 +203,50 @@ struct Consumer {
         acc[r] = a;
       }
     }
+    // halving levels: after them lane l holds row (l >> (5 - log2 RPS))
+    constexpr int LOG = RPS == 16 ? 4 : RPS == 8 ? 3 : RPS == 4 ? 2 : RPS == 2 ? 1 : 0;
 #pragma unroll
-    for (int lvl = 0; lvl < 4; ++lvl) {
-      const int half = 8 >> lvl;       // values kept after this level
-      const int off = 16 >> lvl;       // shuffle distance
+    for (int lvl = 0; lvl < LOG; ++lvl) {
+      const int half = RPS >> (lvl + 1);
+      const int off = 16 >> lvl;
       const bool up = (lane & off) != 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < RPS / 2; ++i) {
         if (i >= half) break;
         const float send = up ? acc[i] : acc[i + half];
         const float keep = up ? acc[i + half] : acc[i];
         acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
       }
     }
-    acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
-    if ((lane & 1) == 0) part[(lane >> 1) & 15] = acc[0];
+    float v = acc[0];
+#pragma unroll
+    for (int off = 16 >> LOG; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if ((lane & ((32 >> LOG) - 1)) == 0) part[lane >> (5 - LOG)] = v;
   }
 
-  // Stream the ns owned GEMV stages of the current instruction. Stage k
-  // multiplies columns [x0(k), x0(k) + 512) of the activation in act[0..K);
-  // partial sums go to part[k * 16 + r]. Returns after a consumer barrier, so
-  // the epilogue may read every partial.
-  template <typename X0>
-  __device__ __forceinline__ void gemv_stream(int ns, int K, float* part, X0 x0_of) {
+  // Stream the ns owned GEMV stages of the current instruction (row segments
+  // of S columns, the activation segment staged at act[0 .. S)). Stage k's row
+  // partials go to part[k * 16 + i]. Returns after a consumer barrier, so the
+  // epilogue may read every partial.
+  __device__ __forceinline__ void gemv_stream(int ns, int S, float* part) {
+    const GemvShape g = gemv_shape(S);
+    const int spb = (16 / g.rps) * g.chunks;
     for (int k = 0; k < ns; ++k) {
-      const uint32_t g = ring.g + k;
-      if (!owns(g)) continue;
-      const uint8_t* st = wait_stage(g);
-      const int x0 = x0_of(k);
-      gemv_stage(st, x0, x0 + 256 < K, part + k * 16);
-      release_owned(g);
+      const uint32_t gi = ring.g + k;
+      if (!owns(gi)) continue;
+      const uint8_t* st = wait_stage(gi);
+      const int c = (k % spb) % g.chunks;
+      const int x0 = c * (STAGE_BYTES / 2);
+      const int len = min(STAGE_BYTES / 2, S - x0);
+      float* out = part + k * 16;
+      switch (g.rps) {
+        case 16: gemv_rows<16>(st, x0, len, out); break;
+        case 8: gemv_rows<8>(st, x0, len, out); break;
+        case 4: gemv_rows<4>(st, x0, len, out); break;
+        case 2: gemv_rows<2>(st, x0, len, out); break;
+        default: gemv_rows<1>(st, x0, len, out); break;
+      }
+      release_owned(gi);
     }
     ring.g += ns;
     sync();
@@ -236,10 +256,13 @@ struct Consumer {
     return reinterpret_cast<float*>(act + ((K * 2 + 15) & ~15));
   }
 
-  // Row r of a block whose stages are part[first .. first + n) (fixed order).
-  __device__ __forceinline__ static float sum_stages(const float* part, int first, int n, int r) {
+  // Row r of the 16-row block whose stages start at part[first * 16] (fixed
+  // summation order over the row's column chunks).
+  __device__ __forceinline__ static float row_sum(const float* part, int first, int S, int r) {
+    const GemvShape g = gemv_shape(S);
+    const int rg = r / g.rps, i = r % g.rps;
     float v = 0.f;
-    for (int s = 0; s < n; ++s) v += part[(first + s) * 16 + r];
+    for (int c = 0; c < g.chunks; ++c) v += part[(first + rg * g.chunks + c) * 16 + i];
     return v;
   }
 
@@ -261,14 +284,14 @@ struct Consumer {
     const int qdim = p.Hq * p.D, kdim = p.Hkv * p.D;
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
-    gemv_stream(pl.ns, p.H, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    gemv_stream(pl.ns, p.H, part);
     stamp(4);
     // one thread per rotary pair (rows 2i, 2i + 1 of a block)
     for (int idx = tid; idx < (b1 - b0) * 8; idx += NC) {
       const int j = idx / 8, pr = idx % 8;
       const int row = (b0 + j) * 16 + 2 * pr;
-      float v0 = bf16r(sum_stages(part, j * spb, spb, 2 * pr));
-      float v1 = bf16r(sum_stages(part, j * spb, spb, 2 * pr + 1));
+      float v0 = bf16r(row_sum(part, j * spb, p.H, 2 * pr));
+      float v1 = bf16r(row_sum(part, j * spb, p.H, 2 * pr + 1));
       if (row < qdim + kdim) {
         // interleaved RoPE (llama.py:136-174) in fp32, rounded to bf16 on store
         const int seg = row % p.D;
@@ -291,7 +314,6 @@ struct Consumer {
     }
     sync();
     if (tid == 0) {
-      __threadfence();
       const int bph = p.D / 16;
       int b = b0;
       while (b < b1) {
@@ -481,7 +503,6 @@ struct Consumer {
     }
     sync();
     if (tid == 0) {
-      __threadfence();
       if (p.skip_red) {
         red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
       } else {
@@ -551,7 +572,6 @@ struct Consumer {
     }
     sync();
     if (tid == 0) {
-      __threadfence();
       red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
     }
   }
@@ -591,12 +611,12 @@ struct Consumer {
     __nv_bfloat16* partials = p.split_partials + (size_t)(o ? 0 : p.o_splits) * p.H;
     const int spb = stages_per_row_block(R);
     float* part = partials_after(R);
-    gemv_stream(pl.ns, R, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    gemv_stream(pl.ns, R, part);
     stamp(4);
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
       const int row = (b0 + j) * 16 + r;
-      const float v = bf16r(sum_stages(part, j * spb, spb, r));
+      const float v = bf16r(row_sum(part, j * spb, R, r));
       if (splits == 1)
         p.hidden[row] = __float2bfloat16_rn(ldcg_bf16(p.hidden + row) + v);
       else
@@ -605,10 +625,7 @@ struct Consumer {
     sync();
     int* done = bar(l, pl.op - 1, 0);
     if (splits == 1) {
-      if (tid == 0) {
-        __threadfence();
-        red_release_add(done, b1 - b0);
-      }
+      if (tid == 0) red_release_add(done, b1 - b0);
       return;
     }
     unsigned* ctrs = p.split_counters + ((size_t)l * 2 + (o ? 0 : 1)) * (p.H / 16);
@@ -649,20 +666,17 @@ struct Consumer {
     stamp(3);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
-    gemv_stream(pl.ns, p.H, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    gemv_stream(pl.ns, p.H, part);
     stamp(4);
     for (int idx = tid; idx < n * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
-      const float u = bf16r(sum_stages(part, j * 2 * spb, spb, r));
-      const float gt = bf16r(sum_stages(part, j * 2 * spb + spb, spb, r));
+      const float u = bf16r(row_sum(part, j * 2 * spb, p.H, r));
+      const float gt = bf16r(row_sum(part, j * 2 * spb + spb, p.H, r));
       const float sl = bf16r(gt / (1.0f + expf(-gt)));
       p.silu[ins.w[3 + j] * 16 + r] = __float2bfloat16_rn(sl * u);
     }
     sync();
-    if (tid == 0) {
-      __threadfence();
-      red_release_add(bar(l, OP_UPGATE - 1, 0), n);
-    }
+    if (tid == 0) red_release_add(bar(l, OP_UPGATE - 1, 0), n);
   }
 
   // RMS_LM_Head (python_vm.py:265-288): logits rows of the final RMSNorm'd hidden.
@@ -678,43 +692,47 @@ struct Consumer {
     stamp(3);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
-    gemv_stream(pl.ns, p.H, part, [&](int k) { return (k % spb) * GEMV_STAGE_COLS; });
+    gemv_stream(pl.ns, p.H, part);
     stamp(4);
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
-      p.logits[(b0 + j) * 16 + r] = __float2bfloat16_rn(sum_stages(part, j * spb, spb, r));
+      p.logits[(b0 + j) * 16 + r] = __float2bfloat16_rn(row_sum(part, j * spb, p.H, r));
     }
   }
 };
 
 // ------------------------------------------------------------------ loader
-// Walks the queue's stage sequence a second time, ahead of the loads, issuing
-// L2 prefetches. Used only while the ring is full, so the prefetches fill HBM
+// A second walk over the queue's stages, ahead of the loads, issuing L2
+// prefetches. It runs only while the ring is full, so the prefetches fill HBM
 // idle time (consumers waiting on other SMs) instead of competing with loads.
 struct PrefetchCursor {
-  int i = 0, k = 0;
+  int i = 0;
   bool have = false;
-  long long g = 0;  // global stage index of (i, k)
+  long long g = 0;  // stream index of the walker's current stage
+  int issued = 0;   // prefetched stages (diagnostics)
   Ins ins;
-  Plan pl;
+  StageWalker wk;
 
-  // Issue the prefetch of the next stage; false when the queue is exhausted.
+  // Prefetch (or skip, if already loaded) one stage; false when exhausted.
   __device__ bool step(const KParams& p, int q, long long g_load) {
     while (true) {
       if (!have) {
         if (i >= p.Q) return false;
         fetch_ins(p, q, i, ins);
-        pl = make_plan(p, ins);
-        k = 0;
+        wk.init(p, ins, make_plan(p, ins));
         have = true;
       }
-      if (k >= pl.ns) {
+      if (wk.done()) {
         ++i;
         have = false;
         continue;
       }
-      if (g >= g_load) do_stage<true>(p, ins, pl, k, nullptr, nullptr);
-      ++k;
+      if (g >= g_load) {
+        wk.issue<true>(p, nullptr, nullptr);
+        ++issued;
+      } else {
+        wk.advance(p);  // already loaded into the ring
+      }
       ++g;
       return true;
     }
@@ -724,6 +742,7 @@ struct PrefetchCursor {
 __device__ void run_loader(const KParams& p, Ring ring) {
   const int q = blockIdx.x;
   Ins ins;
+  StageWalker wk;
   PrefetchCursor pf;
   long long g_load = 0;
   const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
@@ -731,24 +750,29 @@ __device__ void run_loader(const KParams& p, Ring ring) {
   for (int i = 0; i < p.Q; ++i) {
     fetch_ins(p, q, i, ins);
     const Plan pl = make_plan(p, ins);
-    for (int k = 0; k < pl.ns; ++k) {
+    wk.init(p, ins, pl);
+    while (!wk.done()) {
       uint64_t* empty = &ring.empty[ring.slot];
       const uint32_t parity = ring.phase ^ 1u;
-      if (!mbar_try_wait(empty, parity)) {
+      if (!mbar_test_wait(empty, parity)) {
         // ring full: run the L2 prefetch ahead while waiting for a slot
         bool more = p.pf_stages > 0;
-        while (more && pf.g < g_load + p.pf_stages && !mbar_try_wait(empty, parity))
+        while (more && pf.g < g_load + p.pf_stages && !mbar_test_wait(empty, parity))
           more = pf.step(p, q, g_load);
         if (!ring_wait(empty, parity, ring_timeout)) {
           record_error(p, 4, i, pl.op, pl.layer, ring.slot, (int)ring.phase, -1);
           return;
         }
       }
-      do_stage<false>(p, ins, pl, k, ring.stages + (size_t)ring.slot * STAGE_BYTES,
-                      &ring.full[ring.slot]);
+      wk.issue<false>(p, ring.stages + (size_t)ring.slot * STAGE_BYTES, &ring.full[ring.slot]);
       ring_advance(ring);
       ++g_load;
     }
+  }
+  // diagnostics: stages loaded and prefetched by this queue's loader
+  if (p.record && p.timings) {
+    p.timings[(size_t)q * p.Q * 128 + 126] = pf.issued;
+    p.timings[(size_t)q * p.Q * 128 + 127] = (int)g_load;
   }
 }
 
@@ -772,12 +796,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     fence_mbar_init();
   }
   if (tid == NC) {
-    prefetch_tensormap(&p.tm_qkv);
-    prefetch_tensormap(&p.tm_o);
-    prefetch_tensormap(&p.tm_up);
-    prefetch_tensormap(&p.tm_gate);
-    prefetch_tensormap(&p.tm_down);
-    prefetch_tensormap(&p.tm_lm);
     prefetch_tensormap(&p.tm_k);
     prefetch_tensormap(&p.tm_v);
   }

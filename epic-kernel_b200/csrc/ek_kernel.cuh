@@ -41,10 +41,14 @@ constexpr int NTHREADS = NC + 32;     // + loader warp
 constexpr int STAGE_BYTES = 16384;    // one ring stage
 constexpr int HALF_STAGE = 8192;      // one TMA box (16 rows x 256 bf16, or TK x D bf16)
 constexpr int ACT_BYTES = 49152;      // activation vector + per-stage partial sums / attention merge
-constexpr int NUM_STAGES = 11;        // 176 KiB ring
+// Ring slots. Must be a multiple of CW: GEMV stage g is owned by warp g % CW
+// and sits in slot g % NUM_STAGES, so every slot always belongs to the same
+// warp, which visits its laps in order. (With other sizes a fast owner can wait
+// on a slot two laps ahead, where an mbarrier parity wait is ambiguous.)
+constexpr int NUM_STAGES = 8;         // 128 KiB ring
 constexpr int CTRL_BYTES = 1024;      // mbarriers + reduction scratch
 constexpr int SMEM_BYTES = NUM_STAGES * STAGE_BYTES + ACT_BYTES + CTRL_BYTES;
-constexpr int GEMV_STAGE_COLS = 512;  // weight columns per stage (two 256-col boxes)
+static_assert(NUM_STAGES % CW == 0, "ring slots must map to a fixed owner warp");
 constexpr int MAX_GQA = 4;  // query heads per KV head
 
 enum Op : int {
@@ -66,7 +70,15 @@ struct DevStatus {
 };
 
 struct KParams {
-  CUtensorMap tm_qkv, tm_o, tm_up, tm_gate, tm_down, tm_lm, tm_k, tm_v;
+  CUtensorMap tm_k, tm_v;  // KV caches [L*T, Hkv, D], box D x 1 x tk
+
+  const __nv_bfloat16* w_qkv;  // [L * qkv_rows, H]
+  const __nv_bfloat16* w_o;    // [L * H, Hq * D]
+  const __nv_bfloat16* w_up;   // [L * I, H]
+  const __nv_bfloat16* w_gate; // [L * I, H]
+  const __nv_bfloat16* w_down; // [L * H, I]
+  const __nv_bfloat16* w_lm;   // [V, H]
+  long long rows_qkv, rows_o, rows_up, rows_down, rows_lm;  // matrix rows (bounds checks)
 
   int* barriers;
   const int* instructions;
@@ -116,8 +128,33 @@ __device__ __forceinline__ void fetch_ins(const KParams& p, int q, int i, Ins& i
   }
 }
 
-__device__ __forceinline__ int stages_per_row_block(int K) {
-  return (K + GEMV_STAGE_COLS - 1) / GEMV_STAGE_COLS;
+// A GEMV ring stage holds `rps` row segments of up to 8192 bf16 (16 KiB)
+// streamed by 1-D bulk copies: 4 rows of 2048, 2 rows of 3072 or 4096, 8 rows
+// of 1024, 16 rows of 512, or, for segments longer than 8192, one row in
+// `chunks` column chunks (8192 + 6144 for 14336). Segment = the columns of a row
+// an instruction reduces over.
+struct GemvShape {
+  int rps;     // rows per stage (1, 2, 4, 8 or 16)
+  int chunks;  // stages per row segment
+};
+
+__device__ __forceinline__ GemvShape gemv_shape(int S) {
+  GemvShape g;
+  if (S > STAGE_BYTES / 2) {
+    g.rps = 1;
+    g.chunks = (S + STAGE_BYTES / 2 - 1) / (STAGE_BYTES / 2);
+  } else {
+    const int r = (STAGE_BYTES / 2) / S;
+    g.rps = r >= 16 ? 16 : r >= 8 ? 8 : r >= 4 ? 4 : r >= 2 ? 2 : 1;
+    g.chunks = 1;
+  }
+  return g;
+}
+
+// Ring stages per 16-row block for a row segment of S columns.
+__device__ __forceinline__ int stages_per_row_block(int S) {
+  const GemvShape g = gemv_shape(S);
+  return (16 / g.rps) * g.chunks;
 }
 
 // Bytes of `act` a GEMV instruction needs: its activation slice (K bf16) and
@@ -241,78 +278,6 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
 
 // Coordinates of ring stage k of an instruction. `issue` decides between the
 // TMA load into shared memory and the L2 prefetch.
-template <bool PREFETCH>
-__device__ __forceinline__ uint32_t do_stage(const KParams& p, const Ins& ins, const Plan& pl, int k,
-                                             uint8_t* dst, uint64_t* bar) {
-  const int* w = ins.w;
-  const CUtensorMap* map = nullptr;
-  int K = 0, row = 0, col = 0;
-  switch (pl.op) {
-    case OP_QKV: {
-      const int spb = stages_per_row_block(p.H);
-      map = &p.tm_qkv;
-      K = p.H;
-      row = w[1] * p.qkv_rows + (w[2] + k / spb) * 16;
-      col = (k % spb) * GEMV_STAGE_COLS;
-      break;
-    }
-    case OP_OPROJ:
-    case OP_DOWN: {
-      const bool o = pl.op == OP_OPROJ;
-      const int R = o ? p.o_R : p.down_R;
-      const int spb = stages_per_row_block(R);
-      map = o ? &p.tm_o : &p.tm_down;
-      K = (w[4] + 1) * R;
-      row = w[1] * p.H + (w[2] + k / spb) * 16;
-      col = w[4] * R + (k % spb) * GEMV_STAGE_COLS;
-      break;
-    }
-    case OP_UPGATE: {
-      const int spb = stages_per_row_block(p.H);
-      const int j = k / (2 * spb);
-      const int r = k % (2 * spb);
-      map = r < spb ? &p.tm_up : &p.tm_gate;
-      K = p.H;
-      row = w[1] * p.I + w[3 + j] * 16;
-      col = (r % spb) * GEMV_STAGE_COLS;
-      break;
-    }
-    case OP_LM_HEAD: {
-      const int spb = stages_per_row_block(p.H);
-      map = &p.tm_lm;
-      K = p.H;
-      row = (w[1] + k / spb) * 16;
-      col = (k % spb) * GEMV_STAGE_COLS;
-      break;
-    }
-    case OP_PARTIAL: {
-      TokenRange r = partial_tokens(p, w[3], w[4]);
-      const int t0 = w[1] * p.T + r.t_begin + k * p.tk;
-      if (PREFETCH) {
-        tma_prefetch_3d(&p.tm_k, 0, w[2], t0);
-        tma_prefetch_3d(&p.tm_v, 0, w[2], t0);
-      } else {
-        mbar_arrive_expect_tx(bar, 2 * HALF_STAGE);
-        tma_load_3d(dst, &p.tm_k, 0, w[2], t0, bar);
-        tma_load_3d(dst + HALF_STAGE, &p.tm_v, 0, w[2], t0, bar);
-      }
-      return 2 * HALF_STAGE;
-    }
-    default:
-      return 0;
-  }
-  const bool two = col + 256 < K;
-  if (PREFETCH) {
-    tma_prefetch_2d(map, col, row);
-    if (two) tma_prefetch_2d(map, col + 256, row);
-  } else {
-    mbar_arrive_expect_tx(bar, two ? 2 * HALF_STAGE : HALF_STAGE);
-    tma_load_2d(dst, map, col, row, bar);
-    if (two) tma_load_2d(dst + HALF_STAGE, map, col + 256, row, bar);
-  }
-  return two ? 2 * HALF_STAGE : HALF_STAGE;
-}
-
 // ------------------------------------------------------------------ errors
 __device__ __forceinline__ bool aborted(const KParams& p) {
   return ld_relaxed(reinterpret_cast<const int*>(&p.status->abort_epoch)) == (int)p.epoch;
@@ -333,6 +298,125 @@ __device__ inline void record_error(const KParams& p, int code, int instr, int o
   }
   atomicExch(&p.status->abort_epoch, p.epoch);
 }
+
+// Loader-side walk over an instruction's ring stages, in the order the
+// consumers number them (column chunk fastest, then row group, matrix
+// (up, gate), block). Advancing costs a few additions; the per-instruction
+// set-up does the divisions once.
+struct StageWalker {
+  int op, k, ns;
+  // GEMV
+  const __nv_bfloat16* mat[2];
+  long long mat_rows;
+  const int* w;
+  int nmat, stride, col0, S, rps, chunks, groups;  // groups = 16 / rps
+  int j, m, rg, c;
+  long long row_base;  // first matrix row of block j
+  // attention
+  int kv_t0, kv_head;
+
+  __device__ __forceinline__ long long block_row(const KParams& p, int jj) const {
+    switch (op) {
+      case OP_QKV: return (long long)w[1] * p.qkv_rows + (long long)(w[2] + jj) * 16;
+      case OP_OPROJ:
+      case OP_DOWN: return (long long)w[1] * p.H + (long long)(w[2] + jj) * 16;
+      case OP_UPGATE: return (long long)w[1] * p.I + (long long)w[3 + jj] * 16;
+      default: return (long long)(w[1] + jj) * 16;  // OP_LM_HEAD
+    }
+  }
+
+  __device__ __forceinline__ void init(const KParams& p, const Ins& ins, const Plan& pl) {
+    op = pl.op;
+    k = 0;
+    ns = pl.ns;
+    w = ins.w;
+    nmat = 1;
+    col0 = 0;
+    switch (op) {
+      case OP_QKV: mat[0] = p.w_qkv; mat_rows = p.rows_qkv; stride = p.H; S = p.H; break;
+      case OP_OPROJ: mat[0] = p.w_o; mat_rows = p.rows_o; stride = p.Hq * p.D; S = p.o_R; col0 = w[4] * p.o_R; break;
+      case OP_DOWN: mat[0] = p.w_down; mat_rows = p.rows_down; stride = p.I; S = p.down_R; col0 = w[4] * p.down_R; break;
+      case OP_UPGATE: mat[0] = p.w_up; mat[1] = p.w_gate; mat_rows = p.rows_up; nmat = 2; stride = p.H; S = p.H; break;
+      case OP_LM_HEAD: mat[0] = p.w_lm; mat_rows = p.rows_lm; stride = p.H; S = p.H; break;
+      case OP_PARTIAL: {
+        const TokenRange r = partial_tokens(p, w[3], w[4]);
+        kv_t0 = w[1] * p.T + r.t_begin;
+        kv_head = w[2];
+        return;
+      }
+      default: return;
+    }
+    const GemvShape g = gemv_shape(S);
+    rps = g.rps;
+    chunks = g.chunks;
+    groups = 16 / rps;
+    j = m = rg = c = 0;
+    if (ns > 0) row_base = block_row(p, 0);
+  }
+
+  __device__ __forceinline__ bool done() const { return k >= ns; }
+
+  // Issue the current stage (load into dst completing on bar, or an L2
+  // prefetch) and advance. Returns the stage's bytes.
+  template <bool PREFETCH>
+  __device__ __forceinline__ uint32_t issue(const KParams& p, uint8_t* dst, uint64_t* bar) {
+    uint32_t bytes;
+    if (op == OP_PARTIAL) {
+      const int t0 = kv_t0 + k * p.tk;
+      if (PREFETCH) {
+        tma_prefetch_3d(&p.tm_k, 0, kv_head, t0);
+        tma_prefetch_3d(&p.tm_v, 0, kv_head, t0);
+      } else {
+        mbar_arrive_expect_tx(bar, 2 * HALF_STAGE);
+        tma_load_3d(dst, &p.tm_k, 0, kv_head, t0, bar);
+        tma_load_3d(dst + HALF_STAGE, &p.tm_v, 0, kv_head, t0, bar);
+      }
+      bytes = 2 * HALF_STAGE;
+    } else {
+      const int col = col0 + c * (STAGE_BYTES / 2);
+      const int len = min(STAGE_BYTES / 2, S - c * (STAGE_BYTES / 2));
+      const uint32_t row_bytes = (uint32_t)len * 2;
+      bytes = row_bytes * rps;
+      const long long row = row_base + rg * rps;
+      const __nv_bfloat16* src = mat[m] + row * stride + col;
+      const bool whole = len == stride;  // consecutive whole rows: one copy
+      // self-check: rows, columns, size and 16-byte alignment of the copy
+      if (row < 0 || row + rps > mat_rows || col < 0 || col + len > stride || len <= 0 ||
+          bytes > (uint32_t)STAGE_BYTES || ((reinterpret_cast<uintptr_t>(src) | row_bytes) & 15u)) {
+        record_error(p, 5, k, op, (int)(row >> 32), (int)row, col, len);
+        if (!PREFETCH) mbar_arrive_expect_tx(bar, 0);  // completes the phase, no copy
+        advance(p);
+        return 0;
+      }
+      if (PREFETCH) {
+        if (whole) bulk_prefetch_l2(src, bytes);
+        else for (int i = 0; i < rps; ++i) bulk_prefetch_l2(src + (size_t)i * stride, row_bytes);
+      } else {
+        mbar_arrive_expect_tx(bar, bytes);
+        if (whole) bulk_load(dst, src, bytes, bar);
+        else for (int i = 0; i < rps; ++i) bulk_load(dst + i * row_bytes, src + (size_t)i * stride, row_bytes, bar);
+      }
+    }
+    advance(p);
+    return bytes;
+  }
+
+  // Move to the next stage without issuing anything.
+  __device__ __forceinline__ void advance(const KParams& p) {
+    if (op != OP_PARTIAL && ++c == chunks) {
+      c = 0;
+      if (++rg == groups) {
+        rg = 0;
+        if (++m == nmat) {
+          m = 0;
+          ++j;
+          if (k + 1 < ns) row_base = block_row(p, j);
+        }
+      }
+    }
+    ++k;
+  }
+};
 
 // ------------------------------------------------------------------ ring
 struct Ring {

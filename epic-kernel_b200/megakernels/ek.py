@@ -23,6 +23,7 @@ STATUS_NAMES = {
     2: "unknown opcode",
     3: "instruction field out of range",
     4: "load ring stalled",
+    5: "weight copy failed its bounds check",
 }
 
 

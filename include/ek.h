@@ -37,6 +37,7 @@ extern "C" {
 #define EK_STATUS_BAD_OPCODE 2      /* opcode not defined for this model */
 #define EK_STATUS_BAD_INSTRUCTION 3 /* a field of an instruction is out of range */
 #define EK_STATUS_RING_TIMEOUT 4    /* internal load ring stalled (engine bug) */
+#define EK_STATUS_BAD_COPY 5        /* a weight copy failed its bounds check (engine bug) */
 
 typedef struct EkContext EkContext;
 
