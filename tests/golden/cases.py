@@ -8,6 +8,7 @@ import torch
 
 from megakernels.llama import LLAMA3_ROPE_SCALING, LlamaConfig, LlamaForCausalLM
 from megakernels.model_types import ExtraModelConfig
+from megakernels.mixtral.model import MixtralConfig, MixtralForCausalLM
 from megakernels.synthetic import seeded_normal
 
 # 1B-width, 2-layer, 4096-vocab Llama: small enough for the CPU interpreter,
@@ -45,3 +46,21 @@ def fill_kv(k_cache: torch.Tensor, v_cache: torch.Tensor, pos: int, poison: bool
 
 def step_hidden(hidden_size: int, pos: int) -> torch.Tensor:
     return seeded_normal((hidden_size,), HIDDEN_SEED, pos)
+
+
+# Mixtral: FakeModel-like small dims (as the reference's test_mixtral_mk.py),
+# and full-width layers (hidden 4096, 8 experts x 14336) with a small vocab.
+MIXTRAL_SMALL = dict(hidden_size=512, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+                     intermediate_size=1024, num_local_experts=4, num_experts_per_tok=2, vocab_size=256,
+                     rope_theta=1e6, max_position_embeddings=32768)
+MIXTRAL_WIDE = dict(hidden_size=4096, num_hidden_layers=2, num_attention_heads=32, num_key_value_heads=8,
+                    intermediate_size=14336, num_local_experts=8, num_experts_per_tok=2, vocab_size=4096,
+                    rope_theta=1e6, max_position_embeddings=32768)
+MIXTRAL_MAX_LEN = 1024
+MIXTRAL_CASES = (("small", 5), ("small", 300), ("wide", 777))
+
+
+def mixtral_model(name: str, device="cpu"):
+    cfg = MixtralConfig(**(MIXTRAL_SMALL if name == "small" else MIXTRAL_WIDE))
+    return MixtralForCausalLM.random_init(
+        cfg, ExtraModelConfig(interleave_rope=True, max_len_override=MIXTRAL_MAX_LEN), seed=0, device=device)

@@ -56,13 +56,19 @@ def import_reference(ref_root: Path):
 
     ri.get_sm_count = ru.get_sm_count
     rs.get_sm_count = ru.get_sm_count
+    import megakernels.mixtral.scheduler as rms
+    import megakernels.mixtral.python_vm as rmvm
+    import megakernels.mixtral.model as rmm
+
+    rms.get_sm_count = ru.get_sm_count
     import megakernels.llama as rl
     import megakernels.scheduler as rsch
     import megakernels.demos.latency.python_vm as rvm
     import megakernels.generators as rgen
     import megakernels.python_vm as rpy
 
-    return types.SimpleNamespace(llama=rl, sched=rs, base_sched=rsch, vm=rvm, gen=rgen, pyvm=rpy)
+    return types.SimpleNamespace(llama=rl, sched=rs, base_sched=rsch, vm=rvm, gen=rgen, pyvm=rpy,
+                                 mx_sched=rms, mx_vm=rmvm, mx_model=rmm)
 
 
 def reference_model(ref, mine: LlamaForCausalLM, max_len: int):
@@ -196,18 +202,99 @@ def run_1b_greedy(ref, out: dict, prompt_len=128, ntok=64):
     out["1b_threads"] = torch.get_num_threads()
 
 
+def reference_mixtral(ref, mine, max_len: int):
+    """The reference's MixtralForCausalLM carrying the same weights as `mine`."""
+    from transformers import MixtralConfig as HFConfig
+
+    c = mine.config
+    hf = HFConfig(hidden_size=c.hidden_size, num_hidden_layers=c.num_hidden_layers,
+                  num_attention_heads=c.num_attention_heads, num_key_value_heads=c.num_key_value_heads,
+                  intermediate_size=c.intermediate_size, num_local_experts=c.num_local_experts,
+                  num_experts_per_tok=c.num_experts_per_tok, vocab_size=c.vocab_size,
+                  rms_norm_eps=c.rms_norm_eps, rope_theta=c.rope_theta,
+                  max_position_embeddings=c.max_position_embeddings, tie_word_embeddings=False)
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        rm = ref.mx_model.MixtralForCausalLM(
+            hf, ref.llama.ExtraModelConfig(interleave_rope=True, max_len_override=max_len))
+    finally:
+        torch.set_default_dtype(torch.float32)
+    rm.requires_grad_(False)
+    D = c.head_dim
+    inv = torch.empty(D, dtype=torch.long)
+    inv[0::2] = torch.arange(D // 2)
+    inv[1::2] = torch.arange(D // 2) + D // 2
+    undo = torch.argsort(inv)
+    qd, kd = c.num_attention_heads * D, c.num_key_value_heads * D
+    sp = mine.stacked_params
+    for l, blk in enumerate(rm.model.layers):
+        a, moe = blk.self_attn, blk.moe
+        qkv = sp.qkv_proj[l]
+        a.q_proj.weight.copy_(qkv[:qd].view(c.num_attention_heads, D, -1)[:, undo].reshape(qd, -1))
+        a.k_proj.weight.copy_(qkv[qd : qd + kd].view(c.num_key_value_heads, D, -1)[:, undo].reshape(kd, -1))
+        a.v_proj.weight.copy_(qkv[qd + kd :])
+        a.o_proj.weight.copy_(sp.o_proj[l])
+        moe.gate.weight.copy_(sp.router_weight[l])
+        for e, ex in enumerate(moe.experts):
+            ex.w1.weight.copy_(sp.expert_gate[l, e])
+            ex.w3.weight.copy_(sp.expert_up[l, e])
+            ex.w2.weight.copy_(sp.expert_down[l, e])
+    rm.model.embed_tokens.embed_tokens.weight.copy_(mine.model.embed_tokens.embed_tokens.weight)
+    rm.lm_head.lm_head.weight.copy_(mine.lm_head.lm_head.weight)
+    rm.model.interleave_rope()
+    rm.stack_params()
+    rm.setup_caches()
+    assert torch.equal(rm.stacked_params.qkv_proj, sp.qkv_proj), "weight transfer mismatch"
+    assert torch.equal(rm.stacked_params.expert_down, sp.expert_down), "expert transfer mismatch"
+    return rm
+
+
+def run_mixtral(ref, out: dict):
+    arrays = {}
+    models = {}
+    for name, pos in cases.MIXTRAL_CASES:
+        if name not in models:
+            mine = cases.mixtral_model(name)
+            models[name] = (mine, reference_mixtral(ref, mine, cases.MIXTRAL_MAX_LEN))
+            rc = models[name][1].model.rope_cos[: cases.MIXTRAL_MAX_LEN]
+            out[f"mixtral_{name}_rope_cos_maxdiff"] = float((rc - mine.model.rope_cos).abs().max())
+        mine, rm = models[name]
+        sched = ref.mx_sched.MixtralLatencyScheduleBuilder.build(rm, seq_len=pos)
+        g = sched.globs
+        cases.fill_kv(g.k_cache, g.v_cache, pos)
+        g.hidden_states[:] = cases.step_hidden(g.hidden_size, pos)
+        instrs = sched.get_linear_instructions()
+        key = f"{name}_p{pos}"
+        arrays[f"{key}_words"] = np.array(words_of(instrs), dtype=np.int32)
+        t = time.time()
+        ref.pyvm.interpret_with_pyvm(g, instrs, ref.mx_vm.INSTRUCTION_TO_SOLVER)
+        print(f"mixtral {key}: {len(instrs)} instructions, {time.time() - t:.1f}s", flush=True)
+        for n in ("hidden_states", "post_ln_rope_q", "attn_out", "logits", "expert_silu_out",
+                  "selected_expert_scores"):
+            arrays[f"{key}_{n}"] = bf16_bits(getattr(g, n))
+        for n in ("selected_expert_indices", "predicted_expert_indices", "barriers"):
+            arrays[f"{key}_{n}"] = getattr(g, n).numpy().copy()
+        arrays[f"{key}_k_row"] = bf16_bits(g.k_cache[:, 0, pos])
+        arrays[f"{key}_v_row"] = bf16_bits(g.v_cache[:, 0, pos])
+    np.savez_compressed(HERE / "mixtral_step.npz", **arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
     ap.add_argument("--full", action="store_true", help="also run the 192-step Llama-1B case")
+    ap.add_argument("--only", default="", help="llama | mixtral (default: both)")
     args = ap.parse_args()
     ref = import_reference(args.reference)
     info_path = HERE / "golden_info.json"
     out = json.loads(info_path.read_text()) if info_path.exists() else {}
     with torch.no_grad():
-        run_tiny(ref, out)
-        if args.full:
-            run_1b_greedy(ref, out)
+        if args.only in ("", "llama"):
+            run_tiny(ref, out)
+            if args.full:
+                run_1b_greedy(ref, out)
+        if args.only in ("", "mixtral"):
+            run_mixtral(ref, out)
     out["generator"] = "tests/golden/make_golden.py"
     out["sm_count"] = SM_COUNT
     info_path.write_text(json.dumps(out, indent=1, sort_keys=True) + "\n")
