@@ -287,6 +287,8 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   p.pos = a->pos_id; p.skip_red = a->skip_attn_reduction ? 1 : 0;
   p.scale = a->attn_scale; p.eps = a->rms_norm_eps;
   p.down_R = dR; p.o_R = oR; p.down_splits = I / dR; p.o_splits = H / oR;
+  p.model = ek::MODEL_LLAMA;
+  p.down_done_target = (I / dR) * (H / 16);
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
@@ -387,5 +389,112 @@ extern "C" int ek_llama_decode_static(const EkLlamaArgs* a, void* stream, EkStat
   if (status_out &&
       (e = cudaMemcpyAsync(status_out, tmp.status, sizeof(EkStatus), cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
     return cuda_fail(e, "cudaMemcpyAsync(status_out)");
+  return EK_SUCCESS;
+}
+
+extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* stream) {
+  if (!ctx || !a) return fail(EK_E_INVALID, "NULL context or arguments");
+  const void* required[] = {a->barriers, a->instructions, a->qkv_weights, a->attn_ln_weights, a->o_weights,
+                            a->expert_gate_weights, a->expert_up_weights, a->expert_down_weights,
+                            a->router_weights, a->ffn_ln_weights, a->lm_head_norm_weights, a->lm_head_weights,
+                            a->k_cache, a->v_cache, a->rope_cos, a->rope_sin, a->hidden_states, a->q_post_rope,
+                            a->attn_out, a->attn_lse_intermediates, a->attn_out_intermediates,
+                            a->expert_silu_out, a->router_normed_hidden, a->logits};
+  for (size_t i = 0; i < sizeof(required) / sizeof(required[0]); ++i) {
+    if (!required[i]) return fail(EK_E_INVALID, "pointer argument %zu is NULL", i);
+    if (!aligned16(required[i])) return fail(EK_E_INVALID, "pointer argument %zu is not 16-byte aligned", i);
+  }
+  if (!a->selected_expert_indices || !a->selected_expert_scores || !a->predicted_expert_indices)
+    return fail(EK_E_INVALID, "router output pointers must not be NULL");
+  if (a->timings && !aligned16(a->timings)) return fail(EK_E_INVALID, "timings is not 16-byte aligned");
+  const int L = a->num_layers, H = a->hidden, I = a->intermediate, D = a->head_dim;
+  const int Hq = a->num_q_heads, Hkv = a->num_kv_heads, V = a->vocab, E = a->num_experts, K = a->experts_per_token;
+  if (L < 1 || H < 256 || I < 256 || V < 16 || Hq < 1 || Hkv < 1)
+    return fail(EK_E_INVALID, "bad model dims L=%d H=%d I=%d V=%d Hq=%d Hkv=%d", L, H, I, V, Hq, Hkv);
+  if (E < 1 || E > ek::MAX_EXPERTS || K < 1 || K > ek::MAX_TOPK || K > E)
+    return fail(EK_E_UNSUPPORTED, "experts %d / per token %d (max %d / %d)", E, K, ek::MAX_EXPERTS, ek::MAX_TOPK);
+  if (D != 64 && D != 128) return fail(EK_E_UNSUPPORTED, "head_dim %d (supported: 64, 128)", D);
+  if (H % 256 || I % 256) return fail(EK_E_INVALID, "hidden and intermediate must be multiples of 256");
+  if (V % 16) return fail(EK_E_INVALID, "vocab %d not a multiple of 16", V);
+  if (Hq % Hkv || Hq * D != H) return fail(EK_E_INVALID, "heads x head_dim must equal hidden, Hq %% Hkv == 0");
+  const int gqa = Hq / Hkv;
+  if (gqa > ek::MAX_GQA || ek::CW * gqa * (D + 2) * 4 > ek::ACT_BYTES)
+    return fail(EK_E_UNSUPPORTED, "GQA ratio %d too large for head_dim %d", gqa, D);
+  if (I * 2 > ek::ACT_BYTES - 64 * 64) return fail(EK_E_UNSUPPORTED, "intermediate %d too large", I);
+  if (a->kv_len < 1 || a->rope_rows < 1 || a->max_partials < 1)
+    return fail(EK_E_INVALID, "kv_len, rope_rows and max_partials must be positive");
+  if (a->pos_id < 0 || a->pos_id >= a->kv_len || a->pos_id >= a->rope_rows)
+    return fail(EK_E_INVALID, "pos_id %d outside the KV cache or rope table", a->pos_id);
+  if (a->barrier_rows < 8 || a->barrier_cols < Hq + 2 * Hkv || a->barrier_cols < E)
+    return fail(EK_E_INVALID, "barriers must be at least [L, 8, max(Hq + 2 Hkv, E)]");
+  if (a->queue_len < 1 || a->num_queues < 1) return fail(EK_E_INVALID, "empty instruction tensor");
+  DeviceGuard g(ctx->device);
+  int nsm = 0;
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device);
+  if (a->num_queues > nsm) return fail(EK_E_INVALID, "%d instruction queues but only %d SMs", a->num_queues, nsm);
+  int rc = grow(ctx, 1, 1);
+  if (rc) return rc;
+
+  static KParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int qkv_rows = (Hq + 2 * Hkv) * D;
+  const int tk = ek::HALF_STAGE / (D * 2);
+  if ((rc = encode_kv(&p.tm_k, a->k_cache, (long long)L * a->kv_len, Hkv, D, tk, "k_cache"))) return rc;
+  if ((rc = encode_kv(&p.tm_v, a->v_cache, (long long)L * a->kv_len, Hkv, D, tk, "v_cache"))) return rc;
+  p.w_qkv = static_cast<const __nv_bfloat16*>(a->qkv_weights);
+  p.w_o = static_cast<const __nv_bfloat16*>(a->o_weights);
+  p.w_lm = static_cast<const __nv_bfloat16*>(a->lm_head_weights);
+  p.w_egate = static_cast<const __nv_bfloat16*>(a->expert_gate_weights);
+  p.w_eup = static_cast<const __nv_bfloat16*>(a->expert_up_weights);
+  p.w_edown = static_cast<const __nv_bfloat16*>(a->expert_down_weights);
+  p.w_router = static_cast<const __nv_bfloat16*>(a->router_weights);
+  p.ffn_ln = static_cast<const __nv_bfloat16*>(a->ffn_ln_weights);
+  p.rows_qkv = (long long)L * qkv_rows;
+  p.rows_o = (long long)L * H;
+  p.rows_lm = V;
+  p.rows_eup = (long long)L * E * I;
+  p.rows_edown = (long long)L * E * H;
+  p.barriers = a->barriers;
+  p.instructions = a->instructions;
+  p.timings = a->timings;
+  p.attn_ln = static_cast<const __nv_bfloat16*>(a->attn_ln_weights);
+  p.lm_norm = static_cast<const __nv_bfloat16*>(a->lm_head_norm_weights);
+  p.k_cache = static_cast<__nv_bfloat16*>(a->k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(a->v_cache);
+  p.rope_cos = a->rope_cos;
+  p.rope_sin = a->rope_sin;
+  p.hidden = static_cast<__nv_bfloat16*>(a->hidden_states);
+  p.q = static_cast<__nv_bfloat16*>(a->q_post_rope);
+  p.attn_out = static_cast<__nv_bfloat16*>(a->attn_out);
+  p.lse = a->attn_lse_intermediates;
+  p.attn_o = a->attn_out_intermediates;
+  p.expert_silu = static_cast<__nv_bfloat16*>(a->expert_silu_out);
+  p.router_normed = static_cast<__nv_bfloat16*>(a->router_normed_hidden);
+  p.logits = static_cast<__nv_bfloat16*>(a->logits);
+  p.sel_idx = a->selected_expert_indices;
+  p.sel_scores = static_cast<__nv_bfloat16*>(a->selected_expert_scores);
+  p.pred_idx = a->predicted_expert_indices;
+  p.status = ctx->status;
+  p.split_counters = ctx->counters;
+  p.split_partials = ctx->partials;
+  p.model = ek::MODEL_MIXTRAL;
+  p.E = E;
+  p.topk = K;
+  p.down_done_target = K * (H / 16);
+  p.L = L; p.H = H; p.I = I; p.D = D; p.Hq = Hq; p.Hkv = Hkv; p.V = V;
+  p.T = a->kv_len; p.rope_rows = a->rope_rows; p.maxP = a->max_partials;
+  p.brow = a->barrier_rows; p.bcol = a->barrier_cols;
+  p.nq = a->num_queues; p.Q = a->queue_len;
+  p.qkv_rows = qkv_rows; p.gqa = gqa; p.tk = tk;
+  p.pos = a->pos_id; p.skip_red = a->skip_attn_reduction ? 1 : 0;
+  p.scale = a->attn_scale; p.eps = a->rms_norm_eps;
+  p.down_R = I; p.o_R = H; p.down_splits = 1; p.o_splits = 1;
+  p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
+  p.record = a->record_timings && a->timings ? 1 : 0;
+  p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
+  if (++ctx->epoch == 0) ctx->epoch = 1;
+  p.epoch = ctx->epoch;
+  cudaError_t e = ek::launch_decode(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
   return EK_SUCCESS;
 }

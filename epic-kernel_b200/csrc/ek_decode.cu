@@ -17,6 +17,13 @@ struct Consumer {
   uint8_t* act;     // ACT_BYTES: bf16 activation vector or attention merge area
   float* red;       // CW floats of reduction scratch
   int* flag;        // one int broadcast between consumer threads
+  // Mixtral: experts handed to the loader (mbox, completion on mbox_bar) and
+  // router scratch (logits / probabilities, selected experts and scores)
+  int* mbox;
+  uint64_t* mbox_bar;
+  float* rlog;
+  int* rsel;
+  float* rscore;
   int tid, warp, lane;
   int qidx, iidx;   // queue and instruction index (error reports, timings)
   // The ring stalled (an engine bug, reported as EK_STATUS_RING_TIMEOUT). A
@@ -228,7 +235,7 @@ struct Consumer {
   // of S columns, the activation segment staged at act[0 .. S)). Stage k's row
   // partials go to part[k * 16 + i]. Returns after a consumer barrier, so the
   // epilogue may read every partial.
-  __device__ __forceinline__ void gemv_stream(int ns, int S, float* part) {
+  __device__ __forceinline__ void gemv_stream(int ns, int S, float* part, int x_base = 0) {
     const GemvShape g = gemv_shape(S);
     const int spb = (16 / g.rps) * g.chunks;
     for (int k = 0; k < ns; ++k) {
@@ -238,13 +245,14 @@ struct Consumer {
       const int c = (k % spb) % g.chunks;
       const int x0 = c * (STAGE_BYTES / 2);
       const int len = min(STAGE_BYTES / 2, S - x0);
+      const int xc = x_base + x0;
       float* out = part + k * 16;
       switch (g.rps) {
-        case 16: gemv_rows<16>(st, x0, len, out); break;
-        case 8: gemv_rows<8>(st, x0, len, out); break;
-        case 4: gemv_rows<4>(st, x0, len, out); break;
-        case 2: gemv_rows<2>(st, x0, len, out); break;
-        default: gemv_rows<1>(st, x0, len, out); break;
+        case 16: gemv_rows<16>(st, xc, len, out); break;
+        case 8: gemv_rows<8>(st, xc, len, out); break;
+        case 4: gemv_rows<4>(st, xc, len, out); break;
+        case 2: gemv_rows<2>(st, xc, len, out); break;
+        default: gemv_rows<1>(st, xc, len, out); break;
       }
       release_owned(gi);
     }
@@ -272,7 +280,7 @@ struct Consumer {
     const int l = ins.w[1], b0 = ins.w[2], b1 = ins.w[3];
     if (l > 0) {
       int* a = bar(l - 1, OP_DOWN - 1, 0);
-      const int t = p.down_splits * (p.H / 16);
+      const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_QKV, l)) { drain(pl.ns); return; }
     } else if (!wait_counters(0, nullptr, nullptr, OP_QKV, l)) {  // abort check, CTA-uniform
       drain(pl.ns);
@@ -684,7 +692,7 @@ struct Consumer {
     const int b0 = ins.w[1], b1 = ins.w[2];
     {
       int* a = bar(p.L - 1, OP_DOWN - 1, 0);
-      const int t = p.down_splits * (p.H / 16);
+      const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
     }
     stamp(1);
@@ -698,6 +706,191 @@ struct Consumer {
       const int j = idx / 16, r = idx % 16;
       p.logits[(b0 + j) * 16 + r] = __float2bfloat16_rn(row_sum(part, j * spb, p.H, r));
     }
+  }
+  // ---------------------------------------------------------------- Mixtral
+  // Hand the experts of the current expert instruction to the loader (one
+  // handoff per RmsRouterUpgate / ExpertDownProjFused with ring stages).
+  __device__ __forceinline__ void handoff(const int* experts) {
+    if (tid == 0) {
+      for (int i = 0; i < p.topk; ++i) mbox[i] = experts[i];
+      mbar_arrive(mbox_bar);
+    }
+  }
+
+  // Router over the RMSNorm'd hidden in act[0..H) (python_vm.py:541-550):
+  // fp32 logits, softmax, top-k (ties: lower index), scores renormalised over
+  // the top k. Leaves rsel / rscore for every consumer thread.
+  __device__ void router(int l) {
+    const uint4* xs = reinterpret_cast<const uint4*>(act);
+    for (int e = warp; e < p.E; e += CW) {
+      const uint4* wr = reinterpret_cast<const uint4*>(p.w_router + ((size_t)l * p.E + e) * p.H);
+      float d = 0.f;
+      for (int c = lane; c < p.H / 8; c += 32) {
+        const uint4 wv = __ldg(wr + c), xv = xs[c];
+        d = fmaf(bf_lo(wv.x), bf_lo(xv.x), d);
+        d = fmaf(bf_hi(wv.x), bf_hi(xv.x), d);
+        d = fmaf(bf_lo(wv.y), bf_lo(xv.y), d);
+        d = fmaf(bf_hi(wv.y), bf_hi(xv.y), d);
+        d = fmaf(bf_lo(wv.z), bf_lo(xv.z), d);
+        d = fmaf(bf_hi(wv.z), bf_hi(xv.z), d);
+        d = fmaf(bf_lo(wv.w), bf_lo(xv.w), d);
+        d = fmaf(bf_hi(wv.w), bf_hi(xv.w), d);
+      }
+      d = warp_sum(d);
+      if (lane == 0) rlog[e] = d;
+    }
+    sync();
+    if (tid == 0) {
+      float mx = -INFINITY;
+      for (int e = 0; e < p.E; ++e) mx = fmaxf(mx, rlog[e]);
+      float sum = 0.f;
+      for (int e = 0; e < p.E; ++e) {
+        rlog[e] = expf(rlog[e] - mx);
+        sum += rlog[e];
+      }
+      for (int e = 0; e < p.E; ++e) rlog[e] /= sum;
+      float tot = 0.f;
+      for (int i = 0; i < p.topk; ++i) {
+        int best = -1;
+        for (int e = 0; e < p.E; ++e) {
+          bool taken = false;
+          for (int q = 0; q < i; ++q) taken |= rsel[q] == e;
+          if (!taken && (best < 0 || rlog[e] > rlog[best])) best = e;
+        }
+        rsel[i] = best;
+        rscore[i] = rlog[best];
+        tot += rlog[best];
+      }
+      for (int i = 0; i < p.topk; ++i) rscore[i] /= tot;
+    }
+    sync();
+  }
+
+  // RmsRouterUpgate (mixtral/python_vm.py:525-574).
+  __device__ void op_router_upgate(const Ins& ins, const Plan& pl) {
+    const int l = ins.w[1], b0 = ins.w[2], nb = ins.w[3];
+    {
+      int* a = bar(l, OP_OPROJ - 1, 0);
+      const int t = p.H / 16;
+      if (!wait_counters(1, &a, &t, OP_UPGATE, l)) {
+        const int fallback[MAX_TOPK] = {0, 1 % p.E, 2 % p.E, 3 % p.E};
+        if (pl.ns > 0) handoff(fallback);
+        drain(pl.ns);
+        return;
+      }
+    }
+    stamp(1);
+    rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H);
+    router(l);
+    if (pl.ns > 0) handoff(rsel);
+    if (tid < p.topk) {
+      p.sel_idx[tid] = rsel[tid];
+      p.sel_scores[tid] = __float2bfloat16_rn(rscore[tid]);
+    }
+    {
+      const uint4* xs = reinterpret_cast<const uint4*>(act);
+      for (int c = tid; c < p.H / 8; c += NC) reinterpret_cast<uint4*>(p.router_normed)[c] = xs[c];
+    }
+    stamp(3);
+    const int spb = stages_per_row_block(p.H);
+    float* part = partials_after(p.H);
+    gemv_stream(pl.ns, p.H, part);
+    stamp(4);
+    for (int idx = tid; idx < p.topk * nb * 16; idx += NC) {
+      const int es = idx / (nb * 16), j = (idx / 16) % nb, r = idx % 16;
+      const int first = (es * nb + j) * 2 * spb;
+      const float gt = bf16r(row_sum(part, first, p.H, r));
+      const float up = bf16r(row_sum(part, first + spb, p.H, r));
+      const float sl = bf16r(gt / (1.0f + expf(-gt)));
+      p.expert_silu[(size_t)rsel[es] * p.I + (b0 + j) * 16 + r] = __float2bfloat16_rn(sl * up);
+    }
+    sync();
+    if (tid == 0) red_release_add(bar(l, OP_UPGATE - 1, 0), nb);
+  }
+
+  // ExpertDownProjFused (mixtral/python_vm.py:581-611): per selected expert in
+  // top-k order, hidden += bf16(score * bf16(W_down[e][rows] . silu[e])).
+  __device__ void op_expert_down(const Ins& ins, const Plan& pl) {
+    const int l = ins.w[1], b0 = ins.w[2], b1 = ins.w[3], nb = b1 - b0;
+    {
+      int* a = bar(l, OP_UPGATE - 1, 0);
+      const int t = p.I / 16;
+      if (!wait_counters(1, &a, &t, OP_DOWN, l)) {
+        const int fallback[MAX_TOPK] = {0, 1 % p.E, 2 % p.E, 3 % p.E};
+        if (pl.ns > 0) handoff(fallback);
+        drain(pl.ns);
+        return;
+      }
+    }
+    stamp(1);
+    if (tid < p.topk) {
+      int e = __ldcg(p.sel_idx + tid);
+      rsel[tid] = (e < 0 || e >= p.E) ? 0 : e;
+      rscore[tid] = ldcg_bf16(p.sel_scores + tid);
+    }
+    sync();
+    if (pl.ns > 0) handoff(rsel);
+    const int spb = stages_per_row_block(p.I);
+    const int nse = nb * spb;
+    float* part = partials_after(p.I);
+    for (int es = 0; es < p.topk; ++es) {
+      copy_to_act(p.expert_silu + (size_t)rsel[es] * p.I, p.I);
+      gemv_stream(nse, p.I, part + es * nse * 16);
+    }
+    stamp(4);
+    for (int idx = tid; idx < nb * 16; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      const int row = (b0 + j) * 16 + r;
+      float h = ldcg_bf16(p.hidden + row);
+      for (int es = 0; es < p.topk; ++es) {
+        const float v = bf16r(row_sum(part + es * nse * 16, j * spb, p.I, r));
+        h = bf16r(h + bf16r(rscore[es] * v));
+      }
+      p.hidden[row] = __float2bfloat16_rn(h);
+    }
+    sync();
+    if (tid == 0) red_release_add(bar(l, OP_DOWN - 1, 0), nb * p.topk);
+  }
+
+  // Mixtral_RMS_LM_Head (mixtral/python_vm.py:618-642): logits[rows] += bf16
+  // partial over one 2048-column split (bf16 atomic add; the caller zeroes
+  // logits, and with two splits the sum is independent of their order).
+  __device__ void op_lm_head_split(const Ins& ins, const Plan& pl) {
+    const int b0 = ins.w[1], b1 = ins.w[2], split = ins.w[3];
+    {
+      int* a = bar(p.L - 1, OP_DOWN - 1, 0);
+      const int t = p.down_done_target;
+      if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
+    }
+    stamp(1);
+    rmsnorm_to_act(p.hidden, p.lm_norm, p.H);
+    stamp(3);
+    const int spb = stages_per_row_block(LM_HEAD_SPLIT);
+    float* part = partials_after(p.H);
+    gemv_stream(pl.ns, LM_HEAD_SPLIT, part, split * LM_HEAD_SPLIT);
+    stamp(4);
+    for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      atomicAdd(p.logits + (b0 + j) * 16 + r, __float2bfloat16_rn(row_sum(part, j * spb, LM_HEAD_SPLIT, r)));
+    }
+  }
+
+  // SpeculativeExpertPredict (mixtral/python_vm.py:653-668).
+  __device__ void op_predict(const Ins& ins) {
+    const int l = ins.w[1];
+    if (l > 0) {
+      int* a = bar(l - 1, OP_DOWN - 1, 0);
+      const int t = p.down_done_target;
+      if (!wait_counters(1, &a, &t, OP_PREDICT, l)) return;
+    } else if (!wait_counters(0, nullptr, nullptr, OP_PREDICT, l)) {
+      return;
+    }
+    stamp(1);
+    rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H);
+    router(l);
+    if (tid < p.topk) p.pred_idx[tid] = rsel[tid];
+    sync();
+    if (tid == 0) red_release_add(bar(l, OP_PREDICT - 1, 0), 1);
   }
 };
 
@@ -719,7 +912,12 @@ struct PrefetchCursor {
       if (!have) {
         if (i >= p.Q) return false;
         fetch_ins(p, q, i, ins);
-        wk.init(p, ins, make_plan(p, ins));
+        // Mixtral expert instructions: the predicted experts (a hint written
+        // by SpeculativeExpertPredict; stale values only cost a wasted prefetch)
+        int pred[MAX_TOPK] = {0, 0, 0, 0};
+        if (p.model == MODEL_MIXTRAL)
+          for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) pred[t] = ld_relaxed(p.pred_idx + t);
+        wk.init(p, ins, make_plan(p, ins), pred);
         have = true;
       }
       if (wk.done()) {
@@ -739,18 +937,33 @@ struct PrefetchCursor {
   }
 };
 
-__device__ void run_loader(const KParams& p, Ring ring) {
+__device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_t* mbox_bar) {
   const int q = blockIdx.x;
   Ins ins;
   StageWalker wk;
   PrefetchCursor pf;
   long long g_load = 0;
+  uint32_t mbox_phase = 0;
   const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
 
   for (int i = 0; i < p.Q; ++i) {
     fetch_ins(p, q, i, ins);
     const Plan pl = make_plan(p, ins);
-    wk.init(p, ins, pl);
+    int ex[MAX_TOPK] = {0, 0, 0, 0};
+    if (p.model == MODEL_MIXTRAL && (pl.op == OP_UPGATE || pl.op == OP_DOWN) && pl.bad_word < 0 && pl.ns > 0) {
+      // which experts to stream is decided by the consumers (router, or the
+      // router outputs of another SM): wait for their handoff, prefetching
+      // ahead into L2 meanwhile
+      while (p.pf_stages > 0 && pf.g < g_load + p.pf_stages && !mbar_test_wait(mbox_bar, mbox_phase))
+        if (!pf.step(p, q, g_load)) break;
+      if (!ring_wait(mbox_bar, mbox_phase, ring_timeout)) {
+        record_error(p, 4, i, pl.op, pl.layer, -1, (int)mbox_phase, -2);
+        return;
+      }
+      mbox_phase ^= 1u;
+      for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) ex[t] = mbox[t];
+    }
+    wk.init(p, ins, pl, ex);
     while (!wk.done()) {
       uint64_t* empty = &ring.empty[ring.slot];
       const uint32_t parity = ring.phase ^ 1u;
@@ -784,8 +997,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   uint8_t* act = smem + NUM_STAGES * STAGE_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(act + ACT_BYTES);
   uint64_t* empty = full + NUM_STAGES;
-  float* red = reinterpret_cast<float*>(empty + NUM_STAGES);
+  uint64_t* mbox_bar = empty + NUM_STAGES;
+  float* red = reinterpret_cast<float*>(mbox_bar + 1);
   int* flag = reinterpret_cast<int*>(red + CW);
+  int* mbox = flag + 1;                        // MAX_TOPK
+  float* rlog = reinterpret_cast<float*>(mbox + MAX_TOPK);  // MAX_EXPERTS
+  int* rsel = reinterpret_cast<int*>(rlog + MAX_EXPERTS);   // MAX_TOPK
+  float* rscore = reinterpret_cast<float*>(rsel + MAX_TOPK);  // MAX_TOPK
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   if (tid == 0) {
@@ -793,6 +1011,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], CW);
     }
+    mbar_init(mbox_bar, 1);
     fence_mbar_init();
   }
   if (tid == NC) {
@@ -803,7 +1022,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
 
   Ring ring{stages, full, empty, 0, 0u, 0u};
   if (warp == CW) {
-    if (lane == 0) run_loader(p, ring);
+    if (lane == 0) run_loader(p, ring, mbox, mbox_bar);
     return;
   }
 
@@ -812,6 +1031,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   c.act = act;
   c.red = red;
   c.flag = flag;
+  c.mbox = mbox;
+  c.mbox_bar = mbox_bar;
+  c.rlog = rlog;
+  c.rsel = rsel;
+  c.rscore = rscore;
   c.tid = tid;
   c.warp = warp;
   c.lane = lane;
@@ -826,9 +1050,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     c.stamp(0);
     if (pl.bad_word >= 0) {
       if (tid == 0)
-        record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > OP_LM_HEAD) ? 2 : 3, i, pl.op,
+        record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > (p.model == MODEL_MIXTRAL ? OP_PREDICT : OP_LM_HEAD)) ? 2 : 3, i, pl.op,
                      pl.layer, 0, pl.bad_word, ins.w[pl.bad_word]);
       continue;  // no stages were planned for it
+    }
+    if (p.model == MODEL_MIXTRAL && pl.op >= OP_UPGATE) {
+      switch (pl.op) {
+        case OP_UPGATE: c.op_router_upgate(ins, pl); break;
+        case OP_DOWN: c.op_expert_down(ins, pl); break;
+        case OP_LM_HEAD: c.op_lm_head_split(ins, pl); break;
+        case OP_PREDICT: c.op_predict(ins); break;
+        default: break;
+      }
+      c.stamp(2);
+      c.sync();
+      continue;
     }
     switch (pl.op) {
       case OP_NOOP: break;

@@ -50,6 +50,9 @@ constexpr int CTRL_BYTES = 1024;      // mbarriers + reduction scratch
 constexpr int SMEM_BYTES = NUM_STAGES * STAGE_BYTES + ACT_BYTES + CTRL_BYTES;
 static_assert(NUM_STAGES % CW == 0, "ring slots must map to a fixed owner warp");
 constexpr int MAX_GQA = 4;  // query heads per KV head
+constexpr int MAX_EXPERTS = 16;
+constexpr int MAX_TOPK = 4;
+constexpr int LM_HEAD_SPLIT = 2048;  // Mixtral LM-head column split (python_vm.py:630)
 
 enum Op : int {
   OP_NOOP = 0,
@@ -60,7 +63,10 @@ enum Op : int {
   OP_UPGATE = 5,
   OP_DOWN = 6,
   OP_LM_HEAD = 7,
+  OP_PREDICT = 8,  // Mixtral SpeculativeExpertPredict
 };
+
+enum Model : int { MODEL_LLAMA = 0, MODEL_MIXTRAL = 1 };
 
 // Device status record; layout of EkStatus followed by the abort word.
 struct DevStatus {
@@ -79,6 +85,19 @@ struct KParams {
   const __nv_bfloat16* w_down; // [L * H, I]
   const __nv_bfloat16* w_lm;   // [V, H]
   long long rows_qkv, rows_o, rows_up, rows_down, rows_lm;  // matrix rows (bounds checks)
+
+  // Mixtral (model == MODEL_MIXTRAL); opcodes 5/6/7 change meaning, 8 is added
+  const __nv_bfloat16* w_egate;   // [L * E * I, H]
+  const __nv_bfloat16* w_eup;     // [L * E * I, H]
+  const __nv_bfloat16* w_edown;   // [L * E * H, I]
+  const __nv_bfloat16* w_router;  // [L * E, H]
+  const __nv_bfloat16* ffn_ln;    // [L, H]
+  __nv_bfloat16* expert_silu;     // [E, I]
+  __nv_bfloat16* router_normed;   // [H]
+  int* sel_idx;                   // [topk]
+  __nv_bfloat16* sel_scores;      // [topk]
+  int* pred_idx;                  // [topk]
+  long long rows_eup, rows_edown;
 
   int* barriers;
   const int* instructions;
@@ -101,6 +120,8 @@ struct KParams {
   unsigned* split_counters;       // [L][2][H/16] epoch-tagged arrival counters
   __nv_bfloat16* split_partials;  // [2][max_splits][H] bf16 partial sums
 
+  int model, E, topk;
+  int down_done_target;  // counter value of a finished layer (Llama: splits * H/16, Mixtral: k * H/16)
   int L, H, I, D, Hq, Hkv, V, T, rope_rows, maxP, brow, bcol, nq, Q;
   int qkv_rows, gqa, tk;
   int pos, skip_red;
@@ -203,6 +224,44 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
     pl.bad_word = idx;
     pl.ns = 0;
   };
+  if (p.model == MODEL_MIXTRAL && pl.op >= OP_UPGATE && pl.op <= OP_PREDICT) {
+    switch (pl.op) {
+      case OP_UPGATE: {  // RmsRouterUpgate: layer, start_block, num_blocks
+        pl.layer = w[1];
+        if (w[1] < 0 || w[1] >= p.L) { bad(1); break; }
+        if (w[2] < 0) { bad(2); break; }
+        if (w[3] < 0 || w[2] + w[3] > p.I / 16) { bad(3); break; }
+        pl.ns = p.topk * w[3] * 2 * stages_per_row_block(p.H);
+        if (gemv_act_bytes(p.H, pl.ns) > ACT_BYTES) { bad(3); break; }
+        break;
+      }
+      case OP_DOWN: {  // ExpertDownProjFused: layer, start_block, end_block, 0
+        pl.layer = w[1];
+        if (w[1] < 0 || w[1] >= p.L) { bad(1); break; }
+        if (w[2] < 0 || w[2] > w[3]) { bad(2); break; }
+        if (w[3] > p.H / 16) { bad(3); break; }
+        if (w[4] != 0) { bad(4); break; }
+        pl.ns = p.topk * (w[3] - w[2]) * stages_per_row_block(p.I);
+        if (gemv_act_bytes(p.I, pl.ns) > ACT_BYTES) { bad(3); break; }
+        break;
+      }
+      case OP_LM_HEAD: {  // Mixtral_RMS_LM_Head: start_block, end_block, split
+        pl.layer = p.L - 1;
+        if (w[1] < 0 || w[1] > w[2]) { bad(1); break; }
+        if (w[2] > p.V / 16) { bad(2); break; }
+        if (w[3] < 0 || (w[3] + 1) * LM_HEAD_SPLIT > p.H) { bad(3); break; }
+        pl.ns = (w[2] - w[1]) * stages_per_row_block(LM_HEAD_SPLIT);
+        if (gemv_act_bytes(p.H, pl.ns) > ACT_BYTES) { bad(2); break; }
+        break;
+      }
+      case OP_PREDICT: {  // SpeculativeExpertPredict: layer
+        pl.layer = w[1];
+        if (w[1] < 0 || w[1] >= p.L) bad(1);
+        break;
+      }
+    }
+    return pl;
+  }
   switch (pl.op) {
     case OP_NOOP:
       break;
@@ -312,10 +371,22 @@ struct StageWalker {
   int nmat, stride, col0, S, rps, chunks, groups;  // groups = 16 / rps
   int j, m, rg, c;
   long long row_base;  // first matrix row of block j
+  int es, ne;                 // expert slot (Mixtral expert ops), slots
+  int experts[MAX_TOPK];
+  int nblocks;
   // attention
   int kv_t0, kv_head;
 
   __device__ __forceinline__ long long block_row(const KParams& p, int jj) const {
+    if (p.model == MODEL_MIXTRAL) {
+      const long long e = (long long)w[1] * p.E + experts[es];
+      switch (op) {
+        case OP_UPGATE: return e * p.I + (long long)(w[2] + jj) * 16;
+        case OP_DOWN: return e * p.H + (long long)(w[2] + jj) * 16;
+        case OP_LM_HEAD: return (long long)(w[1] + jj) * 16;
+        default: break;
+      }
+    }
     switch (op) {
       case OP_QKV: return (long long)w[1] * p.qkv_rows + (long long)(w[2] + jj) * 16;
       case OP_OPROJ:
@@ -325,13 +396,40 @@ struct StageWalker {
     }
   }
 
-  __device__ __forceinline__ void init(const KParams& p, const Ins& ins, const Plan& pl) {
+  // `ex`: the selected (or, for prefetch, predicted) experts of a Mixtral
+  // expert instruction; ignored otherwise.
+  __device__ __forceinline__ void init(const KParams& p, const Ins& ins, const Plan& pl, const int* ex = nullptr) {
     op = pl.op;
     k = 0;
     ns = pl.ns;
     w = ins.w;
     nmat = 1;
     col0 = 0;
+    es = 0;
+    ne = 1;
+    nblocks = 1 << 30;
+    if (p.model == MODEL_MIXTRAL && (op == OP_UPGATE || op == OP_DOWN || op == OP_LM_HEAD)) {
+      if (op == OP_UPGATE) {
+        mat[0] = p.w_egate; mat[1] = p.w_eup; nmat = 2; mat_rows = p.rows_eup;
+        stride = p.H; S = p.H; nblocks = w[3]; ne = p.topk;
+      } else if (op == OP_DOWN) {
+        mat[0] = p.w_edown; mat_rows = p.rows_edown; stride = p.I; S = p.I;
+        nblocks = w[3] - w[2]; ne = p.topk;
+      } else {
+        mat[0] = p.w_lm; mat_rows = p.rows_lm; stride = p.H; S = LM_HEAD_SPLIT; col0 = w[3] * LM_HEAD_SPLIT;
+      }
+      for (int i = 0; i < MAX_TOPK; ++i) {
+        int e = ex ? ex[i < p.topk ? i : 0] : 0;
+        experts[i] = (e < 0 || e >= p.E) ? 0 : e;
+      }
+      const GemvShape g = gemv_shape(S);
+      rps = g.rps;
+      chunks = g.chunks;
+      groups = 16 / rps;
+      j = m = rg = c = 0;
+      if (ns > 0) row_base = block_row(p, 0);
+      return;
+    }
     switch (op) {
       case OP_QKV: mat[0] = p.w_qkv; mat_rows = p.rows_qkv; stride = p.H; S = p.H; break;
       case OP_OPROJ: mat[0] = p.w_o; mat_rows = p.rows_o; stride = p.Hq * p.D; S = p.o_R; col0 = w[4] * p.o_R; break;
@@ -409,7 +507,10 @@ struct StageWalker {
         rg = 0;
         if (++m == nmat) {
           m = 0;
-          ++j;
+          if (++j == nblocks) {  // Mixtral expert ops: next selected expert
+            j = 0;
+            ++es;
+          }
           if (k + 1 < ns) row_base = block_row(p, j);
         }
       }

@@ -69,6 +69,30 @@ class EkLlamaArgs(ctypes.Structure):
     ]
 
 
+class EkMixtralArgs(ctypes.Structure):
+    _fields_ = [
+        ("barriers", _P), ("instructions", _P), ("timings", _P),
+        ("qkv_weights", _P), ("attn_ln_weights", _P), ("o_weights", _P),
+        ("expert_gate_weights", _P), ("expert_up_weights", _P), ("expert_down_weights", _P),
+        ("router_weights", _P), ("ffn_ln_weights", _P),
+        ("lm_head_norm_weights", _P), ("lm_head_weights", _P),
+        ("k_cache", _P), ("v_cache", _P), ("rope_cos", _P), ("rope_sin", _P),
+        ("hidden_states", _P), ("q_post_rope", _P), ("attn_out", _P),
+        ("attn_lse_intermediates", _P), ("attn_out_intermediates", _P),
+        ("expert_silu_out", _P), ("router_normed_hidden", _P), ("logits", _P),
+        ("selected_expert_indices", _P), ("selected_expert_scores", _P), ("predicted_expert_indices", _P),
+        ("num_layers", _I), ("hidden", _I), ("intermediate", _I), ("head_dim", _I),
+        ("num_q_heads", _I), ("num_kv_heads", _I), ("vocab", _I),
+        ("num_experts", _I), ("experts_per_token", _I),
+        ("kv_len", _I), ("rope_rows", _I), ("max_partials", _I),
+        ("barrier_rows", _I), ("barrier_cols", _I), ("num_queues", _I), ("queue_len", _I),
+        ("pos_id", _I), ("attn_scale", ctypes.c_float), ("rms_norm_eps", ctypes.c_float),
+        ("skip_attn_reduction", _I),
+        ("l2_prefetch_stages", _I), ("record_timings", _I),
+        ("timeout_ns", ctypes.c_int64),
+    ]
+
+
 _lib = None
 _lib_lock = threading.Lock()
 
@@ -91,6 +115,7 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.ek_context_destroy.restype = None
         lib.ek_llama_decode.argtypes = [ctypes.c_void_p, ctypes.POINTER(EkLlamaArgs), ctypes.c_void_p]
         lib.ek_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(EkStatus), ctypes.c_int]
+        lib.ek_mixtral_decode.argtypes = [ctypes.c_void_p, ctypes.POINTER(EkMixtralArgs), ctypes.c_void_p]
         if lib.ek_abi_version() != EK_ABI_VERSION:
             raise RuntimeError(f"{p}: ABI {lib.ek_abi_version()} != expected {EK_ABI_VERSION}")
         _lib = lib

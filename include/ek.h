@@ -104,6 +104,57 @@ typedef struct EkLlamaArgs {
   int64_t timeout_ns;           /* bound of every cross-SM wait; <= 0 selects 1 s */
 } EkLlamaArgs;
 
+/*
+ * Arguments of one Mixtral decode step: the tensors of `mk_mixtral(...)`, in
+ * its order (megakernels/mixtral/mk.py:42-96 and the mixtral_globals struct of
+ * demos/mixtral/mixtral.cuh:154-203 in epic-kernel), plus model dimensions.
+ */
+typedef struct EkMixtralArgs {
+  int32_t* barriers;           /* [L, barrier_rows, barrier_cols] int32, zeroed by the caller */
+  const int32_t* instructions; /* [num_queues, queue_len, 32] int32 */
+  int32_t* timings;            /* [num_queues, queue_len, 128] int32, or NULL */
+  const void* qkv_weights;     /* [L, (Hq + 2 Hkv) D, H] */
+  const void* attn_ln_weights; /* [L, H] */
+  const void* o_weights;       /* [L, H, Hq D] */
+  const void* expert_gate_weights; /* [L * E, I, H] */
+  const void* expert_up_weights;   /* [L * E, I, H] */
+  const void* expert_down_weights; /* [L * E, H, I] */
+  const void* router_weights;  /* [L * E, H] */
+  const void* ffn_ln_weights;  /* [L, H] */
+  const void* lm_head_norm_weights; /* [H] */
+  const void* lm_head_weights; /* [V, H] */
+  void* k_cache;               /* [L, kv_len, Hkv, D] */
+  void* v_cache;
+  const float* rope_cos;       /* f32 [rope_rows, D] */
+  const float* rope_sin;
+  void* hidden_states;         /* [H] */
+  void* q_post_rope;           /* [Hq D] */
+  void* attn_out;              /* [Hq D] */
+  float* attn_lse_intermediates; /* f32 [Hq, max_partials] */
+  float* attn_out_intermediates; /* f32 [Hq, max_partials, D] */
+  void* expert_silu_out;       /* [E, I] */
+  void* router_normed_hidden;  /* [H] */
+  void* logits;                /* [V], zeroed by the caller (LM-head splits add into it) */
+  int32_t* selected_expert_indices; /* int32 [topk] */
+  void* selected_expert_scores;     /* bf16 [topk] */
+  int32_t* predicted_expert_indices; /* int32 [topk] */
+
+  int32_t num_layers, hidden, intermediate, head_dim, num_q_heads, num_kv_heads, vocab;
+  int32_t num_experts, experts_per_token;
+  int32_t kv_len, rope_rows, max_partials;
+  int32_t barrier_rows, barrier_cols;
+  int32_t num_queues, queue_len;
+
+  int32_t pos_id;
+  float attn_scale;
+  float rms_norm_eps;
+  int32_t skip_attn_reduction;
+
+  int32_t l2_prefetch_stages;   /* lookahead L2 prefetch (also speculative expert prefetch); 0 = off */
+  int32_t record_timings;
+  int64_t timeout_ns;
+} EkMixtralArgs;
+
 /* ABI version compiled into the library (EK_ABI_VERSION). */
 int ek_abi_version(void);
 
@@ -141,6 +192,13 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* args, void* stream);
  * is given, the call's EkStatus is copied there on `stream` after the kernel.
  */
 int ek_llama_decode_static(const EkLlamaArgs* args, void* stream, EkStatus* status_out);
+
+/*
+ * Mixtral-8x7B decode step. Replaces the pybind entry point `mk_mixtral` of
+ * epic-kernel (demos/mixtral/mixtral.cu:28-94; called from
+ * megakernels/mixtral/mk.py:13-96).
+ */
+int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* args, void* stream);
 
 /* Copy the device status record to `out` (synchronises with all work queued
  * on the context's device). With `clear`, reset it to EK_STATUS_OK. */
