@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kv", type=int, default=2048)
-    ap.add_argument("--model", default="1b", choices=["1b", "3b"])
+    ap.add_argument("--model", default="1b", choices=["1b", "3b", "mixtral"])
     ap.add_argument("--prefetch", type=int, default=0, help="L2 prefetch stages (0 = off)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -61,23 +61,48 @@ def parse():
 
 def model_config(name):
     from megakernels.llama import llama_3_2_1b_config, llama_3_2_3b_config
+    from megakernels.mixtral.model import MixtralConfig
 
-    return llama_3_2_1b_config() if name == "1b" else llama_3_2_3b_config()
+    return {"1b": llama_3_2_1b_config, "3b": llama_3_2_3b_config, "mixtral": MixtralConfig}[name]()
 
 
 def build_model(name, max_len, device):
     from megakernels.llama import LlamaForCausalLM
+    from megakernels.mixtral.model import MixtralForCausalLM
     from megakernels.model_types import ExtraModelConfig
 
-    return LlamaForCausalLM.random_init(
-        model_config(name), ExtraModelConfig(interleave_rope=True, max_len_override=max_len),
-        seed=0, device=device)
+    extra = ExtraModelConfig(interleave_rope=True, max_len_override=max_len)
+    if name == "mixtral":
+        # 46.7 B parameters: drawn on the device (host draws take minutes)
+        host = torch.device(device).type == "cpu"
+        return MixtralForCausalLM.random_init(model_config(name), extra, seed=0, device=device, host_rng=host)
+    return LlamaForCausalLM.random_init(model_config(name), extra, seed=0, device=device)
+
+
+def builder_and_interp(name, prefetch):
+    if name == "mixtral":
+        from megakernels.mixtral.mk import MixtralMK_Interpreter
+        from megakernels.mixtral.scheduler import MixtralLatencyScheduleBuilder
+
+        return MixtralLatencyScheduleBuilder, MixtralMK_Interpreter(l2_prefetch_stages=prefetch)
+    from megakernels.demos.latency.mk import LatencyMK_Interpreter
+    from megakernels.demos.latency.scheduler import LatencyScheduleBuilder
+
+    return LatencyScheduleBuilder, LatencyMK_Interpreter(l2_prefetch_stages=prefetch)
 
 
 def weight_bytes(model) -> int:
+    """Weight bytes one decode step must read: every matrix once; for Mixtral
+    only the k active experts of each layer (plus the router)."""
     sp = model.stacked_params
-    mats = [sp.qkv_proj, sp.o_proj, sp.up_proj, sp.gate_proj, sp.down_proj, model.lm_head.lm_head.weight]
-    return sum(t.numel() * t.element_size() for t in mats)
+    nbytes = lambda t: t.numel() * t.element_size()  # noqa: E731
+    lm = nbytes(model.lm_head.lm_head.weight)
+    if hasattr(sp, "expert_gate"):
+        c = model.config
+        per_expert = (nbytes(sp.expert_gate) + nbytes(sp.expert_up) + nbytes(sp.expert_down)) // c.num_local_experts
+        return (nbytes(sp.qkv_proj) + nbytes(sp.o_proj) + nbytes(sp.router_weight)
+                + per_expert * c.num_experts_per_tok + lm)
+    return sum(nbytes(t) for t in (sp.qkv_proj, sp.o_proj, sp.up_proj, sp.gate_proj, sp.down_proj)) + lm
 
 
 def kv_bytes_per_token(model) -> int:
@@ -245,8 +270,6 @@ def run_reference(args, rank, world):
 
 def run_ours(args, rank, world, local):
     import mk_llama
-    from megakernels.demos.latency.mk import LatencyMK_Interpreter
-    from megakernels.demos.latency.scheduler import LatencyScheduleBuilder
     from megakernels.generators import MK_Generator
     from megakernels.scheduler import assign_to_sms, tensorize_instructions
 
@@ -256,9 +279,9 @@ def run_ours(args, rank, world, local):
     max_len = args.kv + 2 * total + 16
     model = build_model(args.model, max_len, dev)
     fill_kv(model, args.kv)
-    sched = LatencyScheduleBuilder.build(model, seq_len=args.kv + 2 * total)
+    builder, interp = builder_and_interp(args.model, args.prefetch)
+    sched = builder.build(model, seq_len=args.kv + 2 * total)
     tensorize_instructions(sched.globs, assign_to_sms("rr", schedule=sched))
-    interp = LatencyMK_Interpreter(l2_prefetch_stages=args.prefetch)
     gen = MK_Generator(model, interp, sched)
     stream = torch.cuda.current_stream(dev)
     g = sched.globs
@@ -333,7 +356,7 @@ def run_ours(args, rank, world, local):
     achieved = alg_bytes / (mean_kernel_ms * 1e-3) / 1e9
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.model != "mixtral":
         del model, sched, gen
         tps, cores, dt = cpu_decode_sample(args.model, args.kv, args.cpu_sample_tokens)
         cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
@@ -341,7 +364,8 @@ def run_ours(args, rank, world, local):
                          f"through the CPU port of the reference PyVM ({dt:.1f} s)"}
     if rank != 0:
         return
-    workload = f"llama-3.2-{args.model}-kv{args.kv}-decode"
+    workload = (f"mixtral-8x7b-kv{args.kv}-decode" if args.model == "mixtral"
+                else f"llama-3.2-{args.model}-kv{args.kv}-decode")
     line = {
         "metric": METRIC, "value": world * 1000.0 / step_ms, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
@@ -350,7 +374,7 @@ def run_ours(args, rank, world, local):
         "config": {"workload": workload, "kv_len": args.kv, "batch": 1,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2_prefetch_stages": args.prefetch,
-                   "l2": "no flush: 2.5 GB of weights per step >> 126 MB L2"},
+                   "l2": "no flush: the weights read per step (>= 2.5 GB) exceed the 126 MB L2"},
         "gpu_launches": args.steps,
         "ms_per_token_kernel": mean_kernel_ms,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -104,3 +104,27 @@ def test_1b_greedy_tokens_match_reference(golden_dir):
     prefix = ties[0] if ties else N
     assert free[:prefix] == list(expected[:prefix]), (
         f"free-running tokens differ before the first near-tie (step {prefix})")
+
+
+def test_3b_step_kv2048_vs_oracle():
+    """Llama-3.2-3B (head_dim 128, 3 query heads per KV head, 8 down-proj
+    column splits) one step at KV length 2048 against the CPU oracle."""
+    from megakernels.llama import llama_3_2_3b_config
+
+    pos = 2047
+    cfg = llama_3_2_3b_config()
+    extra = ExtraModelConfig(interleave_rope=True, max_len_override=2112)
+    cpu = LlamaForCausalLM.random_init(cfg, extra, seed=0)
+    hidden = cases.step_hidden(cfg.hidden_size, pos)
+    ref, alt = noise_floor(cpu, pos, hidden)
+    del cpu
+    gpu_model = LlamaForCausalLM.random_init(cfg, extra, seed=0, device="cuda")
+    s = prepare(gpu_model, pos, hidden)
+    assert s.globs.matvec_reduction_size == 1024
+    run_gpu(s)
+    import mk_llama
+
+    mk_llama.check()
+    assert torch.equal(s.globs.barriers.cpu(), ref.globs.barriers)
+    mx, rms = assert_logits_within_floor(s.globs.logits, ref.globs.logits, alt.globs.logits)
+    print(f"3B kv2048 logits: max/std {mx:.4f} rms/std {rms:.4f}")
