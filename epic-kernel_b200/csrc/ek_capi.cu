@@ -23,6 +23,15 @@ struct EkContext {
   __nv_bfloat16* partials = nullptr;
   size_t partials_cap = 0;  // elements
   unsigned epoch = 0;
+  // Mixtral tensor parallelism
+  int tp_world = 1, tp_rank = 0;
+  int tp_layers = 0, tp_hidden = 0, tp_topk = 0, tp_vocab = 0;
+  char* tp_buf = nullptr;
+  size_t tp_bytes = 0;
+  char* tp_peer[ek::MAX_TP] = {};
+  bool tp_connected = false;
+  unsigned tp_step = 0;
+  long long off_recv_o = 0, off_recv_d = 0, off_cnt_o = 0, off_cnt_d = 0, off_cnt_lm = 0, off_logits = 0;
 };
 
 namespace {
@@ -169,7 +178,76 @@ void ek_context_destroy(EkContext* ctx) {
   if (ctx->status) cudaFree(ctx->status);
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->partials) cudaFree(ctx->partials);
+  for (int r = 0; r < ctx->tp_world; ++r)
+    if (ctx->tp_peer[r] && r != ctx->tp_rank) cudaIpcCloseMemHandle(ctx->tp_peer[r]);
+  if (ctx->tp_buf) cudaFree(ctx->tp_buf);
   delete ctx;
+}
+
+static long long align256(long long x) { return (x + 255) & ~255ll; }
+
+int ek_tp_setup(EkContext* ctx, int rank, int world, int num_layers, int hidden, int experts_per_token,
+                int full_vocab, void* ipc_handle_out, void** logits_out) {
+  if (!ctx || !ipc_handle_out || !logits_out) return fail(EK_E_INVALID, "NULL argument");
+  if (world < 2 || world > ek::MAX_TP || rank < 0 || rank >= world)
+    return fail(EK_E_INVALID, "rank %d / world %d (2..%d ranks)", rank, world, ek::MAX_TP);
+  if (num_layers < 1 || hidden < 16 || hidden % 16 || experts_per_token < 1 || full_vocab < 16)
+    return fail(EK_E_INVALID, "bad dims");
+  DeviceGuard g(ctx->device);
+  if (ctx->tp_buf) {
+    for (int r = 0; r < ctx->tp_world; ++r)
+      if (ctx->tp_peer[r] && r != ctx->tp_rank) cudaIpcCloseMemHandle(ctx->tp_peer[r]);
+    cudaFree(ctx->tp_buf);
+    ctx->tp_buf = nullptr;
+  }
+  long long off = 0;
+  ctx->off_recv_o = off; off = align256(off + (long long)world * hidden * 4);
+  ctx->off_recv_d = off; off = align256(off + (long long)world * experts_per_token * hidden * 4);
+  ctx->off_cnt_o = off; off = align256(off + (long long)num_layers * (hidden / 16) * 4);
+  ctx->off_cnt_d = off; off = align256(off + (long long)num_layers * (hidden / 16) * 4);
+  ctx->off_cnt_lm = off; off = align256(off + 16);
+  ctx->off_logits = off; off = align256(off + (long long)full_vocab * 2);
+  cudaError_t e;
+  if ((e = cudaMalloc(&ctx->tp_buf, off)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(tp buffer)");
+  if ((e = cudaMemset(ctx->tp_buf, 0, off)) != cudaSuccess) return cuda_fail(e, "cudaMemset(tp buffer)");
+  cudaIpcMemHandle_t h;
+  if ((e = cudaIpcGetMemHandle(&h, ctx->tp_buf)) != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  std::memcpy(ipc_handle_out, &h, 64);
+  *logits_out = ctx->tp_buf + ctx->off_logits;
+  ctx->tp_bytes = off;
+  ctx->tp_world = world;
+  ctx->tp_rank = rank;
+  ctx->tp_layers = num_layers;
+  ctx->tp_hidden = hidden;
+  ctx->tp_topk = experts_per_token;
+  ctx->tp_vocab = full_vocab;
+  ctx->tp_connected = false;
+  ctx->tp_step = 0;
+  for (int r = 0; r < ek::MAX_TP; ++r) ctx->tp_peer[r] = nullptr;
+  return EK_SUCCESS;
+}
+
+int ek_tp_connect(EkContext* ctx, const void* ipc_handles) {
+  if (!ctx || !ipc_handles) return fail(EK_E_INVALID, "NULL argument");
+  if (!ctx->tp_buf) return fail(EK_E_INVALID, "ek_tp_setup first");
+  DeviceGuard g(ctx->device);
+  const char* hs = static_cast<const char*>(ipc_handles);
+  for (int r = 0; r < ctx->tp_world; ++r) {
+    if (r == ctx->tp_rank) {
+      ctx->tp_peer[r] = ctx->tp_buf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hs + 64 * r, 64);
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    ctx->tp_peer[r] = static_cast<char*>(ptr);
+  }
+  ctx->tp_connected = true;
+  ctx->tp_step = 0;
+  return EK_SUCCESS;
 }
 
 int ek_read_status(EkContext* ctx, EkStatus* out, int clear) {
@@ -327,6 +405,15 @@ struct StaticScratch {
   unsigned* counters = nullptr;
   __nv_bfloat16* partials = nullptr;
   unsigned epoch = 0;
+  // Mixtral tensor parallelism
+  int tp_world = 1, tp_rank = 0;
+  int tp_layers = 0, tp_hidden = 0, tp_topk = 0, tp_vocab = 0;
+  char* tp_buf = nullptr;
+  size_t tp_bytes = 0;
+  char* tp_peer[ek::MAX_TP] = {};
+  bool tp_connected = false;
+  unsigned tp_step = 0;
+  long long off_recv_o = 0, off_recv_d = 0, off_cnt_o = 0, off_cnt_d = 0, off_cnt_lm = 0, off_logits = 0;
 };
 
 std::mutex g_static_mu;
@@ -416,7 +503,17 @@ extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* s
   if (D != 64 && D != 128) return fail(EK_E_UNSUPPORTED, "head_dim %d (supported: 64, 128)", D);
   if (H % 256 || I % 256) return fail(EK_E_INVALID, "hidden and intermediate must be multiples of 256");
   if (V % 16) return fail(EK_E_INVALID, "vocab %d not a multiple of 16", V);
-  if (Hq % Hkv || Hq * D != H) return fail(EK_E_INVALID, "heads x head_dim must equal hidden, Hq %% Hkv == 0");
+  const bool tp = ctx->tp_connected && ctx->tp_world > 1;
+  if (Hq % Hkv) return fail(EK_E_INVALID, "num_q_heads %% num_kv_heads != 0");
+  if (!tp && Hq * D != H) return fail(EK_E_INVALID, "num_q_heads * head_dim must equal hidden");
+  if ((Hq * D) % 256) return fail(EK_E_INVALID, "num_q_heads * head_dim must be a multiple of 256");
+  if (tp) {
+    if (L != ctx->tp_layers || H != ctx->tp_hidden || K != ctx->tp_topk || V * ctx->tp_world != ctx->tp_vocab)
+      return fail(EK_E_INVALID, "dims differ from ek_tp_setup");
+    if (a->logits != ctx->tp_buf + ctx->off_logits)
+      return fail(EK_E_INVALID, "with tensor parallelism, logits must be the context's symmetric buffer");
+    if (a->tp_lm_instructions < 0) return fail(EK_E_INVALID, "tp_lm_instructions < 0");
+  }
   const int gqa = Hq / Hkv;
   if (gqa > ek::MAX_GQA || ek::CW * gqa * (D + 2) * 4 > ek::ACT_BYTES)
     return fail(EK_E_UNSUPPORTED, "GQA ratio %d too large for head_dim %d", gqa, D);
@@ -488,7 +585,22 @@ extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* s
   p.qkv_rows = qkv_rows; p.gqa = gqa; p.tk = tk;
   p.pos = a->pos_id; p.skip_red = a->skip_attn_reduction ? 1 : 0;
   p.scale = a->attn_scale; p.eps = a->rms_norm_eps;
-  p.down_R = I; p.o_R = H; p.down_splits = 1; p.o_splits = 1;
+  p.down_R = I; p.o_R = Hq * D; p.down_splits = 1; p.o_splits = 1;
+  p.tp_world = 1;
+  if (tp) {
+    p.tp_world = ctx->tp_world;
+    p.tp_rank = ctx->tp_rank;
+    for (int r = 0; r < ctx->tp_world; ++r) p.tp_peer[r] = ctx->tp_peer[r];
+    p.tp_off_recv_o = ctx->off_recv_o;
+    p.tp_off_recv_d = ctx->off_recv_d;
+    p.tp_off_cnt_o = ctx->off_cnt_o;
+    p.tp_off_cnt_d = ctx->off_cnt_d;
+    p.tp_off_cnt_lm = ctx->off_cnt_lm;
+    p.tp_off_logits = ctx->off_logits;
+    p.lm_row0 = ctx->tp_rank * V;
+    p.tp_lm_count = a->tp_lm_instructions;
+    p.tp_step = ++ctx->tp_step;
+  }
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;

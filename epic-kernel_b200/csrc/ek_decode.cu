@@ -88,15 +88,16 @@ struct Consumer {
   //
   // Thread 0 spins until every counter in `addrs` reaches its target, bounded
   // by p.timeout_ns. Returns (to all consumer threads) whether to run the op.
-  __device__ bool wait_counters(int n, int* const* addrs, const int* targets, int opcode, int layer) {
+  __device__ bool wait_counters(int n, int* const* addrs, const int* targets, int opcode, int layer,
+                                bool sys_scope = false) {
     if (tid == 0) {
       int ok = 1;
       for (int j = 0; j < n && ok; ++j) {
-        int v = ld_acquire(addrs[j]);
+        int v = sys_scope ? ld_acquire_sys(addrs[j]) : ld_acquire(addrs[j]);
         if (v >= targets[j]) continue;
         const uint64_t t0 = globaltimer();
         for (uint32_t it = 0;; ++it) {
-          v = ld_acquire(addrs[j]);
+          v = sys_scope ? ld_acquire_sys(addrs[j]) : ld_acquire(addrs[j]);
           if (v >= targets[j]) break;
           if ((it & 15u) == 15u) {
             if (aborted(p)) { ok = 0; break; }
@@ -621,6 +622,28 @@ struct Consumer {
     float* part = partials_after(R);
     gemv_stream(pl.ns, R, part);
     stamp(4);
+    if (o && p.tp_world > 1) {
+      // tensor parallel: all-reduce the fp32 row partials over NVLink, then
+      // add their rank-ordered sum, rounded once, to hidden (same on all ranks)
+      for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+        const int j = idx / 16, r = idx % 16;
+        const int row = (b0 + j) * 16 + r;
+        const float v = row_sum(part, j * spb, R, r);
+        for (int rk = 0; rk < p.tp_world; ++rk) tp_slot(rk, p.tp_off_recv_o)[(size_t)p.tp_rank * p.H + row] = v;
+      }
+      sync();
+      if (!tp_exchange(p.tp_off_cnt_o, l, b0, b1, OP_OPROJ)) return;
+      const float* recv = tp_slot(p.tp_rank, p.tp_off_recv_o);
+      for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+        const int row = b0 * 16 + idx;
+        float sum = 0.f;
+        for (int rk = 0; rk < p.tp_world; ++rk) sum += __ldcg(recv + (size_t)rk * p.H + row);
+        p.hidden[row] = __float2bfloat16_rn(ldcg_bf16(p.hidden + row) + bf16r(sum));
+      }
+      sync();
+      if (tid == 0) red_release_add(bar(l, OP_OPROJ - 1, 0), b1 - b0);
+      return;
+    }
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
       const int row = (b0 + j) * 16 + r;
@@ -707,6 +730,32 @@ struct Consumer {
       p.logits[(b0 + j) * 16 + r] = __float2bfloat16_rn(row_sum(part, j * spb, p.H, r));
     }
   }
+  // ---------------------------------------------------------------- tensor parallel
+  __device__ __forceinline__ float* tp_slot(int rank, long long off) const {
+    return reinterpret_cast<float*>(p.tp_peer[rank] + off);
+  }
+  __device__ __forceinline__ int* tp_counter(int rank, long long off, int idx) const {
+    return reinterpret_cast<int*>(p.tp_peer[rank] + off) + idx;
+  }
+
+  // Signal every rank that this rank pushed blocks [b0, b1) of layer l (one
+  // counter per 16-row block), then wait until all ranks pushed them here.
+  // Call after a consumer barrier that follows the pushes.
+  __device__ bool tp_exchange(long long cnt_off, int l, int b0, int b1, int opcode) {
+    if (tid == 0) {
+      __threadfence_system();
+      for (int r = 0; r < p.tp_world; ++r)
+        for (int b = b0; b < b1; ++b) red_release_sys_add(tp_counter(r, cnt_off, l * (p.H / 16) + b), 1);
+    }
+    bool ok = true;
+    const int target = p.tp_world * (int)p.tp_step;
+    for (int b = b0; b < b1 && ok; ++b) {
+      int* a = tp_counter(p.tp_rank, cnt_off, l * (p.H / 16) + b);
+      ok = wait_counters(1, &a, &target, opcode, l, true);
+    }
+    return ok;
+  }
+
   // ---------------------------------------------------------------- Mixtral
   // Hand the experts of the current expert instruction to the loader (one
   // handoff per RmsRouterUpgate / ExpertDownProjFused with ring stages).
@@ -838,6 +887,29 @@ struct Consumer {
       gemv_stream(nse, p.I, part + es * nse * 16);
     }
     stamp(4);
+    if (p.tp_world > 1) {
+      // tensor parallel: all-reduce each expert's fp32 row partials
+      for (int idx = tid; idx < p.topk * nb * 16; idx += NC) {
+        const int es = idx / (nb * 16), j = (idx / 16) % nb, r = idx % 16;
+        const int row = (b0 + j) * 16 + r;
+        const float v = row_sum(part + es * nse * 16, j * spb, p.I, r);
+        for (int rk = 0; rk < p.tp_world; ++rk)
+          tp_slot(rk, p.tp_off_recv_d)[((size_t)p.tp_rank * p.topk + es) * p.H + row] = v;
+      }
+      sync();
+      if (!tp_exchange(p.tp_off_cnt_d, l, b0, b1, OP_DOWN)) return;
+      const float* recv = tp_slot(p.tp_rank, p.tp_off_recv_d);
+      for (int idx = tid; idx < nb * 16; idx += NC) {
+        const int row = b0 * 16 + idx;
+        float h = ldcg_bf16(p.hidden + row);
+        for (int es = 0; es < p.topk; ++es) {
+          float sum = 0.f;
+          for (int rk = 0; rk < p.tp_world; ++rk) sum += __ldcg(recv + ((size_t)rk * p.topk + es) * p.H + row);
+          h = bf16r(h + bf16r(rscore[es] * bf16r(sum)));
+        }
+        p.hidden[row] = __float2bfloat16_rn(h);
+      }
+    } else {
     for (int idx = tid; idx < nb * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
       const int row = (b0 + j) * 16 + r;
@@ -847,6 +919,7 @@ struct Consumer {
         h = bf16r(h + bf16r(rscore[es] * v));
       }
       p.hidden[row] = __float2bfloat16_rn(h);
+    }
     }
     sync();
     if (tid == 0) red_release_add(bar(l, OP_DOWN - 1, 0), nb * p.topk);
@@ -869,6 +942,22 @@ struct Consumer {
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, LM_HEAD_SPLIT, part, split * LM_HEAD_SPLIT);
     stamp(4);
+    if (p.tp_world > 1) {
+      // tensor parallel: this rank's vocabulary rows go into every rank's logits
+      for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+        const int j = idx / 16, r = idx % 16;
+        const __nv_bfloat16 v = __float2bfloat16_rn(row_sum(part, j * spb, LM_HEAD_SPLIT, r));
+        const int row = p.lm_row0 + (b0 + j) * 16 + r;
+        for (int rk = 0; rk < p.tp_world; ++rk)
+          atomicAdd(reinterpret_cast<__nv_bfloat16*>(p.tp_peer[rk] + p.tp_off_logits) + row, v);
+      }
+      sync();
+      if (tid == 0) {
+        __threadfence_system();
+        for (int rk = 0; rk < p.tp_world; ++rk) red_release_sys_add(tp_counter(rk, p.tp_off_cnt_lm, 0), 1);
+      }
+      return;
+    }
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
       atomicAdd(p.logits + (b0 + j) * 16 + r, __float2bfloat16_rn(row_sum(part, j * spb, LM_HEAD_SPLIT, r)));
@@ -1079,6 +1168,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     }
     c.stamp(2);
     c.sync();  // act / red / flag are reused by the next instruction
+  }
+  // tensor parallel: the logits are complete once every rank's LM-head
+  // instructions have added into them; block 0 holds the kernel until then
+  if (p.model == MODEL_MIXTRAL && p.tp_world > 1 && p.tp_lm_count > 0 && blockIdx.x == 0) {
+    int* a = c.tp_counter(p.tp_rank, p.tp_off_cnt_lm, 0);
+    const int t = p.tp_world * p.tp_lm_count * (int)p.tp_step;
+    c.iidx = p.Q;
+    c.wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1, true);
   }
 }
 

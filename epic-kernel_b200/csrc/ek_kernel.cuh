@@ -52,7 +52,8 @@ static_assert(NUM_STAGES % CW == 0, "ring slots must map to a fixed owner warp")
 constexpr int MAX_GQA = 4;  // query heads per KV head
 constexpr int MAX_EXPERTS = 16;
 constexpr int MAX_TOPK = 4;
-constexpr int LM_HEAD_SPLIT = 2048;  // Mixtral LM-head column split (python_vm.py:630)
+constexpr int LM_HEAD_SPLIT = 2048;
+constexpr int MAX_TP = 8;  // Mixtral LM-head column split (python_vm.py:630)
 
 enum Op : int {
   OP_NOOP = 0,
@@ -98,6 +99,14 @@ struct KParams {
   __nv_bfloat16* sel_scores;      // [topk]
   int* pred_idx;                  // [topk]
   long long rows_eup, rows_edown;
+
+  // Mixtral tensor parallelism (tp_world > 1): symmetric buffers of all ranks
+  int tp_world, tp_rank;
+  unsigned tp_step;          // launches since ek_tp_connect (counters are cumulative)
+  char* tp_peer[8];          // base of each rank's symmetric buffer (tp_peer[tp_rank] = own)
+  long long tp_off_recv_o, tp_off_recv_d, tp_off_cnt_o, tp_off_cnt_d, tp_off_cnt_lm, tp_off_logits;
+  int lm_row0;               // first global vocabulary row of this rank's LM-head shard
+  int tp_lm_count;           // LM-head instructions per rank and launch
 
   int* barriers;
   const int* instructions;

@@ -90,6 +90,7 @@ class EkMixtralArgs(ctypes.Structure):
         ("skip_attn_reduction", _I),
         ("l2_prefetch_stages", _I), ("record_timings", _I),
         ("timeout_ns", ctypes.c_int64),
+        ("tp_lm_instructions", _I),
     ]
 
 
@@ -116,6 +117,9 @@ def load_library(path: Path | str | None = None) -> ctypes.CDLL:
         lib.ek_llama_decode.argtypes = [ctypes.c_void_p, ctypes.POINTER(EkLlamaArgs), ctypes.c_void_p]
         lib.ek_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(EkStatus), ctypes.c_int]
         lib.ek_mixtral_decode.argtypes = [ctypes.c_void_p, ctypes.POINTER(EkMixtralArgs), ctypes.c_void_p]
+        lib.ek_tp_setup.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.ek_tp_connect.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
         if lib.ek_abi_version() != EK_ABI_VERSION:
             raise RuntimeError(f"{p}: ABI {lib.ek_abi_version()} != expected {EK_ABI_VERSION}")
         _lib = lib

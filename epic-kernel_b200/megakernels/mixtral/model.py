@@ -42,10 +42,12 @@ class MixtralConfig:
     rope_scaling: dict | None = None
     max_position_embeddings: int = 32768
     tie_word_embeddings: bool = False
+    # set on tensor-parallel shards, whose local head count no longer divides hidden
+    head_dim_override: int | None = None
 
     @property
     def head_dim(self) -> int:
-        return self.hidden_size // self.num_attention_heads
+        return self.head_dim_override or self.hidden_size // self.num_attention_heads
 
 
 @dataclass
@@ -84,21 +86,58 @@ class MixtralForCausalLM(nn.Module):
 
     @classmethod
     def random_init(cls, config: MixtralConfig, extra_config: ExtraModelConfig | None = None, seed: int = 0,
-                    std: float = 0.02, device="cpu", dtype=torch.bfloat16, host_rng: bool = True):
+                    std: float = 0.02, device="cpu", dtype=torch.bfloat16, host_rng: bool = True,
+                    tp: tuple[int, int] | None = None):
+        """With `tp=(rank, world)` the model is that rank's tensor-parallel
+        shard of the same weights: query/KV heads, expert intermediate rows
+        (gate/up rows, down columns) and LM-head vocabulary rows are split
+        evenly; router, norms and the embedding are replicated."""
+        full = config
+        rank, world = tp if tp else (0, 1)
+        if world > 1:
+            assert full.num_attention_heads % world == 0 and full.num_key_value_heads % world == 0
+            assert full.intermediate_size % world == 0 and full.vocab_size % world == 0
+            config = MixtralConfig(**{**full.__dict__,
+                                      "num_attention_heads": full.num_attention_heads // world,
+                                      "num_key_value_heads": full.num_key_value_heads // world,
+                                      "intermediate_size": full.intermediate_size // world,
+                                      "vocab_size": full.vocab_size // world,
+                                      "head_dim_override": full.head_dim})
         m = cls(config, extra_config, device=device, dtype=dtype)
         c = config
         D, H, L, E, I = c.head_dim, c.hidden_size, c.num_hidden_layers, c.num_local_experts, c.intermediate_size
         qd, kd = c.num_attention_heads * D, c.num_key_value_heads * D
+        fqd, fkd, fI, fV = full.num_attention_heads * D, full.num_key_value_heads * D, full.intermediate_size, full.vocab_size
         dev = m.device
         gen = None
         if not host_rng:
             gen = torch.Generator(device=dev)
             gen.manual_seed(seed)
 
-        def w(shape, tid):
+        def draw(shape, tid):
             if host_rng:
                 return seeded_normal(shape, seed, tid, std, dtype).to(dev)
             return torch.empty(shape, dtype=dtype, device=dev).normal_(0, std, generator=gen)
+
+        def rows(n_full):  # this rank's slice of a split dimension
+            n = n_full // world
+            return slice(rank * n, (rank + 1) * n)
+
+        # full-shape draws, sliced to this rank's shard (kind from the tensor id)
+        def w(shape, tid):
+            k = tid % 64 if tid < _EMBED else tid
+            if k in (_Q, _K, _V):
+                n_full = fqd if k == _Q else fkd
+                return draw((n_full, H), tid)[rows(n_full)]
+            if k == _O:
+                return draw((H, fqd), tid)[:, rows(fqd)].contiguous()
+            if _GATE <= k < _DOWN:  # gate and up rows
+                return draw((fI, H), tid)[rows(fI)]
+            if _DOWN <= k < _DOWN + 16:
+                return draw((H, fI), tid)[:, rows(fI)].contiguous()
+            if k == _LM:
+                return draw((fV, H), tid)[rows(fV)]
+            return draw(shape, tid)
 
         def stacked(shape_fn, tid_fn):
             out = torch.empty((L, E) + shape_fn, dtype=dtype, device=dev)
@@ -118,7 +157,7 @@ class MixtralForCausalLM(nn.Module):
             expert_up=stacked((I, H), lambda l, e: 64 * l + _UP + e),
             expert_down=stacked((H, I), lambda l, e: 64 * l + _DOWN + e),
         )
-        m.model.embed_tokens.embed_tokens.weight.data = w((c.vocab_size, H), _EMBED)
+        m.model.embed_tokens.embed_tokens.weight.data = draw((fV, H), _EMBED)  # replicated, full vocabulary
         m.lm_head.lm_head.weight.data = w((c.vocab_size, H), _LM)
         m.lm_head.input_norm.weight.data = m.lm_head.input_norm.weight.data.to(dev)
         cos, sin = rope_tables(D, c.rope_theta, c.rope_scaling, m.max_len())

@@ -53,7 +53,9 @@ def make_globals(model, skip_attn_reduction: bool | None = None, seq_len: int = 
         return torch.zeros(shape, device=device, dtype=buf_dtype)
 
     E = config.num_local_experts
-    head_dim = config.hidden_size // config.num_attention_heads
+    # = hidden / heads (reference scheduler.py:70); explicit on tensor-parallel shards
+    head_dim = getattr(config, "head_dim", config.hidden_size // config.num_attention_heads)
+    qdim = config.num_attention_heads * head_dim
     max_parts = get_sm_count(device)
     empty = torch.empty(0, device=device, dtype=dtype)
     return MixtralGlobals(
@@ -85,8 +87,8 @@ def make_globals(model, skip_attn_reduction: bool | None = None, seq_len: int = 
             dtype=torch.int32, device=device),
         pos_id=seq_len,
         hidden_states=buf(config.hidden_size),
-        post_ln_rope_q=buf(config.hidden_size),
-        attn_out=buf(config.hidden_size),
+        post_ln_rope_q=buf(qdim),
+        attn_out=buf(qdim),
         attn_out_intermediates=buf([config.num_attention_heads, max_parts, head_dim], torch.float32),
         attn_lse_intermediates=buf([config.num_attention_heads, max_parts], torch.float32),
         expert_silu_out=buf([E, config.intermediate_size]),

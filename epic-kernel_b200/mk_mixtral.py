@@ -8,7 +8,8 @@ weights flattened to [L * E, ...], router [L * E, H], FFN norms, LM head
 outputs, then pos_id, attn_scale, rms_norm_eps, skip_attn_reduction, and
 `stream=`. Keyword-only options: l2_prefetch_stages (lookahead L2 prefetch,
 which also prefetches the predicted experts of expert instructions),
-record_timings, timeout_ns.
+record_timings, timeout_ns, tp_lm_instructions (tensor parallel: LM-head
+instructions per rank, set by megakernels.mixtral.tp).
 """
 
 import ctypes
@@ -22,7 +23,7 @@ _BF16 = torch.bfloat16
 _cache: dict = {}
 
 
-def _build(t, l2_prefetch_stages, record_timings, timeout_ns):
+def _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions=0):
     (barriers, instructions, timings, qkv_w, attn_ln_w, o_w, eg, eu, ed, router_w, ffn_ln_w, lm_norm, lm_w,
      k4, v4, cos, sin, hidden, q, attn_out, lse, o_int, esilu, rnormed, logits, sel, scores, pred) = t
     a = ek.EkMixtralArgs()
@@ -87,6 +88,7 @@ def _build(t, l2_prefetch_stages, record_timings, timeout_ns):
     a.l2_prefetch_stages = l2_prefetch_stages
     a.record_timings = int(bool(record_timings))
     a.timeout_ns = int(timeout_ns)
+    a.tp_lm_instructions = int(tp_lm_instructions)
     return a, hidden.device.index
 
 
@@ -101,6 +103,7 @@ def mk_mixtral(
     selected_expert_indices, selected_expert_scores, predicted_expert_indices,
     pos_id, attn_scale, rms_norm_eps, skip_attn_reduction,
     *, stream=None, l2_prefetch_stages: int = 0, record_timings: bool = False, timeout_ns: int = 0,
+    tp_lm_instructions: int = 0,
 ):
     t = (barriers, instructions, timings, qkv_weights, attn_norm_weights, o_weights, expert_gate_weights,
          expert_up_weights, expert_down_weights, router_weights, ffn_ln_weights, lm_head_norm_weights,
@@ -108,10 +111,10 @@ def mk_mixtral(
          attn_lse_intermediates, attn_out_intermediates, expert_silu_out, router_normed_hidden, logits,
          selected_expert_indices, selected_expert_scores, predicted_expert_indices)
     key = (tuple((x.data_ptr(), tuple(x.shape), x.dtype) if x is not None else None for x in t),
-           l2_prefetch_stages, bool(record_timings), int(timeout_ns))
+           l2_prefetch_stages, bool(record_timings), int(timeout_ns), int(tp_lm_instructions))
     hit = _cache.get(key)
     if hit is None:
-        hit = _build(t, l2_prefetch_stages, record_timings, timeout_ns)
+        hit = _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions)
         if len(_cache) > 64:
             _cache.clear()
         _cache[key] = hit

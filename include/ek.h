@@ -153,6 +153,11 @@ typedef struct EkMixtralArgs {
   int32_t l2_prefetch_stages;   /* lookahead L2 prefetch (also speculative expert prefetch); 0 = off */
   int32_t record_timings;
   int64_t timeout_ns;
+
+  /* tensor parallel (after ek_tp_connect): this rank holds num_q_heads /
+   * num_kv_heads / intermediate / vocab of its shard; `logits` must be the
+   * context's symmetric logits buffer (full vocabulary, vocab * world rows). */
+  int32_t tp_lm_instructions;   /* Mixtral_RMS_LM_Head instructions in this rank's queues */
 } EkMixtralArgs;
 
 /* ABI version compiled into the library (EK_ABI_VERSION). */
@@ -199,6 +204,24 @@ int ek_llama_decode_static(const EkLlamaArgs* args, void* stream, EkStatus* stat
  * megakernels/mixtral/mk.py:13-96).
  */
 int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* args, void* stream);
+
+/*
+ * Tensor parallelism for Mixtral (no counterpart in the reference, whose
+ * megakernel is single-GPU; SURVEY row e). Each rank calls ek_tp_setup, which
+ * allocates the rank's symmetric buffer (receive slots for the fp32 row
+ * partials of O-proj and of the expert down projection, arrival counters, the
+ * full-vocabulary logits) and returns its CUDA IPC handle (64 bytes) and the
+ * device address of its logits. The handles are exchanged out of band
+ * (torch.distributed) and passed, in rank order, to ek_tp_connect. After that,
+ * ek_mixtral_decode all-reduces the hidden state inside the kernel: partials
+ * are pushed with plain NVLink stores, counters bumped with release.sys
+ * atomics, waits are bounded, and every rank sums in rank order, so all ranks
+ * hold bit-identical states. A failed launch leaves the counters inconsistent:
+ * set up again after one.
+ */
+int ek_tp_setup(EkContext* ctx, int rank, int world, int num_layers, int hidden, int experts_per_token,
+                int full_vocab, void* ipc_handle_out, void** logits_out);
+int ek_tp_connect(EkContext* ctx, const void* ipc_handles);
 
 /* Copy the device status record to `out` (synchronises with all work queued
  * on the context's device). With `clear`, reset it to EK_STATUS_OK. */

@@ -64,3 +64,21 @@ def mixtral_model(name: str, device="cpu"):
     cfg = MixtralConfig(**(MIXTRAL_SMALL if name == "small" else MIXTRAL_WIDE))
     return MixtralForCausalLM.random_init(
         cfg, ExtraModelConfig(interleave_rope=True, max_len_override=MIXTRAL_MAX_LEN), seed=0, device=device)
+
+
+def fill_kv_shard(k_cache, v_cache, pos: int, rank: int, world: int):
+    """fill_kv for a tensor-parallel shard: the full-model KV draws, sliced to
+    this rank's KV heads."""
+    L, B, T, h, D = k_cache.shape
+    full_k = torch.zeros(L, B, T, h * world, D, dtype=k_cache.dtype)
+    full_v = torch.zeros_like(full_k)
+    fill_kv(full_k, full_v, pos)
+    k_cache.copy_(full_k[:, :, :, rank * h : (rank + 1) * h])
+    v_cache.copy_(full_v[:, :, :, rank * h : (rank + 1) * h])
+
+
+def mixtral_shard(name: str, rank: int, world: int, device="cpu"):
+    cfg = MixtralConfig(**(MIXTRAL_SMALL if name == "small" else MIXTRAL_WIDE))
+    return MixtralForCausalLM.random_init(
+        cfg, ExtraModelConfig(interleave_rope=True, max_len_override=MIXTRAL_MAX_LEN), seed=0, device=device,
+        tp=(rank, world))
