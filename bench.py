@@ -1,7 +1,7 @@
 """Batch-1 decode benchmark: Llama-3.2-1B (random-init bf16) at KV length 2048.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--kv 2048] [--model 1b|3b] [--prefetch S]
+                    [--kv 2048] [--model 1b|3b|mixtral] [--prefetch S]
 
 A step is one decode token: embed, barrier reset, one megakernel launch over
 the whole model, argmax. The output token feeds the next step, as in
@@ -10,8 +10,10 @@ no L2 flush is needed between steps.
 
 One JSON line is printed by rank 0:
 - `value`: tokens/s with all inputs resident in HBM (device-timed, CUDA events,
-  max over ranks). For N > 1 each rank runs an independent replica, so the
-  scaling is weak and `value` sums over ranks.
+  max over ranks). For N > 1 each Llama rank runs an independent replica, so
+  the scaling is weak and `value` sums over ranks; Mixtral runs tensor
+  parallel over the N GPUs (one token stream, strong scaling, in-kernel
+  NVLink all-reduce), so `value` is that stream's tokens/s.
 - `e2e`: the same metric through the public API with host buffers. Every step
   copies the input token from pinned host memory and reads the output token
   back to the host.
@@ -66,7 +68,7 @@ def model_config(name):
     return {"1b": llama_3_2_1b_config, "3b": llama_3_2_3b_config, "mixtral": MixtralConfig}[name]()
 
 
-def build_model(name, max_len, device):
+def build_model(name, max_len, device, tp=None):
     from megakernels.llama import LlamaForCausalLM
     from megakernels.mixtral.model import MixtralForCausalLM
     from megakernels.model_types import ExtraModelConfig
@@ -75,11 +77,17 @@ def build_model(name, max_len, device):
     if name == "mixtral":
         # 46.7 B parameters: drawn on the device (host draws take minutes)
         host = torch.device(device).type == "cpu"
-        return MixtralForCausalLM.random_init(model_config(name), extra, seed=0, device=device, host_rng=host)
+        return MixtralForCausalLM.random_init(model_config(name), extra, seed=0, device=device, host_rng=host,
+                                              tp=tp)
     return LlamaForCausalLM.random_init(model_config(name), extra, seed=0, device=device)
 
 
-def builder_and_interp(name, prefetch):
+def builder_and_interp(name, prefetch, tp=False):
+    if name == "mixtral" and tp:
+        from megakernels.mixtral.scheduler import MixtralLatencyScheduleBuilder
+        from megakernels.mixtral.tp import MixtralTPMK_Interpreter
+
+        return MixtralLatencyScheduleBuilder, MixtralTPMK_Interpreter(l2_prefetch_stages=prefetch)
     if name == "mixtral":
         from megakernels.mixtral.mk import MixtralMK_Interpreter
         from megakernels.mixtral.scheduler import MixtralLatencyScheduleBuilder
@@ -110,13 +118,13 @@ def kv_bytes_per_token(model) -> int:
     return c.num_hidden_layers * 2 * c.num_key_value_heads * c.head_dim * 2
 
 
-def fill_kv(model, kv):
+def fill_kv(model, kv, rank=0):
     from megakernels.synthetic import seeded_normal
 
     k, v = model.stacked_kv_cache
     L, B, _, H, D = k.shape
     for i, c in enumerate((k, v)):
-        c[:, :, :kv] = seeded_normal((L, B, kv, H, D), 1, 7000 + i).to(c.device)
+        c[:, :, :kv] = seeded_normal((L, B, kv, H, D), 1, 7000 + 16 * rank + i).to(c.device)
 
 
 def load_peaks():
@@ -277,10 +285,15 @@ def run_ours(args, rank, world, local):
     torch.cuda.set_device(dev)
     total = args.warmup + args.steps
     max_len = args.kv + 2 * total + 16
-    model = build_model(args.model, max_len, dev)
-    fill_kv(model, args.kv)
-    builder, interp = builder_and_interp(args.model, args.prefetch)
+    tp = args.model == "mixtral" and world > 1  # Mixtral shards; Llama runs replicas
+    model = build_model(args.model, max_len, dev, tp=(rank, world) if tp else None)
+    fill_kv(model, args.kv, rank)
+    builder, interp = builder_and_interp(args.model, args.prefetch, tp)
     sched = builder.build(model, seq_len=args.kv + 2 * total)
+    if tp:
+        from megakernels.mixtral.tp import setup_tensor_parallel
+
+        setup_tensor_parallel(sched.globs, rank, world)
     tensorize_instructions(sched.globs, assign_to_sms("rr", schedule=sched))
     gen = MK_Generator(model, interp, sched)
     stream = torch.cuda.current_stream(dev)
@@ -366,13 +379,14 @@ def run_ours(args, rank, world, local):
         return
     workload = (f"mixtral-8x7b-kv{args.kv}-decode" if args.model == "mixtral"
                 else f"llama-3.2-{args.model}-kv{args.kv}-decode")
+    streams = 1 if tp else world  # token streams the job decodes at once
     line = {
-        "metric": METRIC, "value": world * 1000.0 / step_ms, "unit": "tokens/s",
+        "metric": METRIC, "value": streams * 1000.0 / step_ms, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights N(0,0.02) seed 0; KV N(0,1) seed 1)",
         "config": {"workload": workload, "kv_len": args.kv, "batch": 1,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "parallelism": (f"tp{world}" if tp else f"replicas{world}") if world > 1 else "single",
                    "l2_prefetch_stages": args.prefetch,
                    "l2": "no flush: the weights read per step (>= 2.5 GB) exceed the 126 MB L2"},
         "gpu_launches": args.steps,
@@ -380,9 +394,10 @@ def run_ours(args, rank, world, local):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": alg_bytes,
+                     "scope": "per GPU: this rank's shard" if tp else "per GPU",
                      "traffic": read_profile_traffic(workload)},
         "clocks": clocks.summary(),
-        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "tokens/s",
+        "e2e": {"value": streams * 1000.0 / e2e_ms, "unit": "tokens/s",
                 "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
         "cpu_baseline": cpu,
     }
