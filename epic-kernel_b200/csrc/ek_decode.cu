@@ -10,6 +10,137 @@
 
 namespace ek {
 
+// ------------------------------------------------------------------ GEMV streaming
+// The GEMV inner loop, as free functions taking the ring state by value (so the
+// consumer's state stays in registers; one out-of-line copy per variant).
+//
+// A stage holds RPS row segments of `len` columns (row i at st + i * len * 2);
+// consumer thread t takes its 16-byte pieces t + 256 j (j < 4), whose column
+// piece within the row is pc[j] and whose row is rowj[j] (warp-uniform:
+// len % 256 == 0). Each thread keeps one fp32 accumulator per row of the 16-row
+// block; at the end of the block the warp reduce-scatters the 16 rows and
+// writes part[blk * BLOCK_PART + row * CW + warp]. Fixed summation order:
+// within a thread, stages and pieces in stream order; then a fixed shuffle
+// tree; then warps in order (row_sum).
+
+// Bounded wait for a ring stage, per thread (no warp vote on the fast path):
+// the clock is read only every 1024 polls. On timeout the thread records the
+// stall, marks itself broken and stops waiting on the ring.
+__device__ __forceinline__ void stage_wait(const KParams& p, uint64_t* bar, uint32_t parity, long long timeout,
+                                           uint32_t& broken, int iidx, int slot) {
+  if (broken || mbar_try_wait(bar, parity)) return;
+  uint64_t t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return;
+    if ((it & 1023u) == 0) {
+      const uint64_t now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if ((long long)(now - t0) > timeout) {
+        record_error(p, 4, iidx, -1, -1, slot, (int)parity, threadIdx.x >> 5);
+        broken = 1;
+        return;
+      }
+    }
+  }
+}
+
+// RPS: rows per stage. ROW_IS_J: S == 2048, so piece j of every thread lies in
+// row j of the stage at column piece tid. FULL: every stage holds 1024 pieces.
+// Only RPS == 1 splits rows into column chunks.
+template <int RPS, bool ROW_IS_J, bool FULL>
+__device__ __noinline__ uint2 gemv_blocks_rps(const KParams& p, const uint8_t* stages, uint64_t* full,
+                                              uint64_t* empty, uint32_t g, uint32_t broken, const uint8_t* act,
+                                              int nblk, int chunks, int S, int x_base, float* part,
+                                              uint32_t timing, int iidx) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ppr = min(S, STAGE_BYTES / 2) / 8;
+  int pc[4], rowj[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int P = tid + 256 * j;
+    rowj[j] = (RPS == 1 || ROW_IS_J) ? 0 : P / ppr;
+    pc[j] = RPS == 1 ? P : ROW_IS_J ? tid : P - rowj[j] * ppr;
+  }
+  const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
+  uint32_t slot = g % NUM_STAGES, parity = (g / NUM_STAGES) & 1u;
+  const uint4* xs4 = reinterpret_cast<const uint4*>(act) + x_base / 8;
+  const int nch = RPS == 1 ? chunks : 1;
+  int k = 0;
+  for (int blk = 0; blk < nblk; ++blk) {
+    float acc[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int rg = 0; rg < 16 / RPS; ++rg) {
+      for (int c = 0; c < nch; ++c, ++k) {
+        stage_wait(p, &full[slot], parity, ring_timeout, broken, iidx, (int)slot);
+        if (timing != 0xffffffffu && tid == 0 && k < 28)
+          p.timings[(size_t)timing * 128 + 8 + k] = (int)(globaltimer() & 0x7fffffff);
+        const uint4* w4 = reinterpret_cast<const uint4*>(stages + (size_t)slot * STAGE_BYTES);
+        const int x0 = c * (STAGE_BYTES / 2);
+        const int npieces = FULL ? 1024 : RPS * (min(STAGE_BYTES / 2, S - x0) / 8);
+        const uint4* xc = xs4 + x0 / 8;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (!FULL && tid + 256 * j >= npieces) continue;  // warp-uniform
+          const float d = dot8_bf16(w4[tid + 256 * j], xc[pc[j]], 0.f);
+          if (RPS == 1) {
+            acc[rg] += d;
+          } else if (ROW_IS_J) {
+            acc[rg * RPS + j] += d;
+          } else {
+#pragma unroll
+            for (int q = 0; q < RPS; ++q) acc[rg * RPS + q] += rowj[j] == q ? d : 0.f;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == NUM_STAGES) {
+          slot = 0;
+          parity ^= 1u;
+        }
+      }
+    }
+    // reduce-scatter: after 4 halving levels lane l holds row l >> 1
+#pragma unroll
+    for (int lvl = 0; lvl < 4; ++lvl) {
+      const int half = 8 >> lvl;
+      const int off = 16 >> lvl;
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i >= half) break;
+        const float send = up ? acc[i] : acc[i + half];
+        const float keep = up ? acc[i + half] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    const float v = acc[0] + __shfl_xor_sync(0xffffffffu, acc[0], 1);
+    if ((lane & 1) == 0) part[blk * BLOCK_PART + (lane >> 1) * CW + warp] = v;
+  }
+  return make_uint2(g + (uint32_t)k, broken);
+}
+
+// Returns (ring index after the instruction's stages, broken flag).
+__device__ __forceinline__ uint2 gemv_blocks(const KParams& p, const uint8_t* stages, uint64_t* full,
+                                             uint64_t* empty, uint32_t g, bool broken, const uint8_t* act,
+                                             int nblk, int S, int x_base, float* part, uint32_t timing,
+                                             int iidx) {
+  const GemvShape sh = gemv_shape(S);
+  const uint32_t b = broken ? 1u : 0u;
+#define EK_GEMV(R, J, F) \
+  gemv_blocks_rps<R, J, F>(p, stages, full, empty, g, b, act, nblk, sh.chunks, S, x_base, part, timing, iidx)
+  switch (sh.rps) {
+    case 16: return S == 512 ? EK_GEMV(16, false, true) : EK_GEMV(16, false, false);
+    case 8: return S == 1024 ? EK_GEMV(8, false, true) : EK_GEMV(8, false, false);
+    case 4: return S == 2048 ? EK_GEMV(4, true, true) : EK_GEMV(4, false, false);
+    case 2: return S == 4096 ? EK_GEMV(2, false, true) : EK_GEMV(2, false, false);
+    default: return S % 8192 == 0 ? EK_GEMV(1, false, true) : EK_GEMV(1, false, false);
+  }
+#undef EK_GEMV
+}
+
 // ------------------------------------------------------------------ consumer helpers
 struct Consumer {
   const KParams& p;
@@ -36,10 +167,8 @@ struct Consumer {
   __device__ __forceinline__ void sync() { named_sync<NC>(); }
 
   // Ring stages are numbered in stream order (ring.g); stage g lives in slot
-  // g % NUM_STAGES with phase parity (g / NUM_STAGES) & 1. A stage is either
-  // shared (every consumer warp reads it and arrives once on its empty
-  // barrier, used by attention) or owned by warp (g % CW), which arrives for
-  // all CW warps (used by the GEMVs).
+  // g % NUM_STAGES with phase parity (g / NUM_STAGES) & 1. Every consumer warp
+  // reads every stage and arrives once on its empty barrier (count CW).
   __device__ __forceinline__ const uint8_t* wait_stage(uint32_t g) {
     const int slot = g % NUM_STAGES;
     if (!broken) {
@@ -61,24 +190,12 @@ struct Consumer {
     ++ring.g;
   }
 
-  // Owned stage g: the owner warp frees it for everyone.
-  __device__ __forceinline__ void release_owned(uint32_t g) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive_cnt(&ring.empty[g % NUM_STAGES], CW);
-  }
-
-  __device__ __forceinline__ bool owns(uint32_t g) const { return (int)(g % CW) == warp; }
-
-  // Skip ns stages without computing (aborted launch): owners free them.
+  // Skip ns stages without computing (aborted launch).
   __device__ void drain(int ns) {
     for (int k = 0; k < ns; ++k) {
-      const uint32_t g = ring.g + k;
-      if (owns(g)) {
-        wait_stage(g);
-        release_owned(g);
-      }
+      acquire();
+      release();
     }
-    ring.g += ns;
   }
 
   // Publication rule: every consumer thread writes its results, the consumer
@@ -179,85 +296,18 @@ struct Consumer {
     sync();
   }
 
-  // One owned GEMV stage: RPS row segments of `len` columns (row i at
-  // st + i * len * 2) times act[xcol0 .. xcol0 + len). Lanes stride over 16-byte
-  // pieces, so every shared-memory load is conflict-free and each activation
-  // piece serves all RPS rows. The RPS row sums are then reduce-scattered over
-  // the warp and written to part[0 .. RPS).
-  template <int RPS>
-  __device__ __forceinline__ void gemv_rows(const uint8_t* st, int xcol0, int len, float* part) {
-    const uint4* xs4 = reinterpret_cast<const uint4*>(act) + xcol0 / 8;
-    float acc[RPS];
-#pragma unroll
-    for (int r = 0; r < RPS; ++r) acc[r] = 0.f;
-    const int pieces = len / 8;
-#pragma unroll 2
-    for (int pc = lane; pc < pieces; pc += 32) {
-      const uint4 xv = xs4[pc];
-      const float x[8] = {bf_lo(xv.x), bf_hi(xv.x), bf_lo(xv.y), bf_hi(xv.y),
-                          bf_lo(xv.z), bf_hi(xv.z), bf_lo(xv.w), bf_hi(xv.w)};
-#pragma unroll
-      for (int r = 0; r < RPS; ++r) {
-        const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)r * len * 2 + pc * 16);
-        float a = acc[r];
-        a = fmaf(bf_lo(w.x), x[0], a);
-        a = fmaf(bf_hi(w.x), x[1], a);
-        a = fmaf(bf_lo(w.y), x[2], a);
-        a = fmaf(bf_hi(w.y), x[3], a);
-        a = fmaf(bf_lo(w.z), x[4], a);
-        a = fmaf(bf_hi(w.z), x[5], a);
-        a = fmaf(bf_lo(w.w), x[6], a);
-        a = fmaf(bf_hi(w.w), x[7], a);
-        acc[r] = a;
-      }
-    }
-    // halving levels: after them lane l holds row (l >> (5 - log2 RPS))
-    constexpr int LOG = RPS == 16 ? 4 : RPS == 8 ? 3 : RPS == 4 ? 2 : RPS == 2 ? 1 : 0;
-#pragma unroll
-    for (int lvl = 0; lvl < LOG; ++lvl) {
-      const int half = RPS >> (lvl + 1);
-      const int off = 16 >> lvl;
-      const bool up = (lane & off) != 0;
-#pragma unroll
-      for (int i = 0; i < RPS / 2; ++i) {
-        if (i >= half) break;
-        const float send = up ? acc[i] : acc[i + half];
-        const float keep = up ? acc[i + half] : acc[i];
-        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-      }
-    }
-    float v = acc[0];
-#pragma unroll
-    for (int off = 16 >> LOG; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    if ((lane & ((32 >> LOG) - 1)) == 0) part[lane >> (5 - LOG)] = v;
-  }
-
-  // Stream the ns owned GEMV stages of the current instruction (row segments
-  // of S columns, the activation segment staged at act[0 .. S)). Stage k's row
-  // partials go to part[k * 16 + i]. Returns after a consumer barrier, so the
-  // epilogue may read every partial.
+  // Stream the ns GEMV stages of the current instruction (whole 16-row blocks
+  // of S-column row segments; the activation segment staged at
+  // act[x_base .. x_base + S)). Block b's partials go to part[b * BLOCK_PART ..].
+  // Returns after a consumer barrier, so the epilogue may read every partial.
   __device__ __forceinline__ void gemv_stream(int ns, int S, float* part, int x_base = 0) {
     const GemvShape g = gemv_shape(S);
-    const int spb = (16 / g.rps) * g.chunks;
-    for (int k = 0; k < ns; ++k) {
-      const uint32_t gi = ring.g + k;
-      if (!owns(gi)) continue;
-      const uint8_t* st = wait_stage(gi);
-      const int c = (k % spb) % g.chunks;
-      const int x0 = c * (STAGE_BYTES / 2);
-      const int len = min(STAGE_BYTES / 2, S - x0);
-      const int xc = x_base + x0;
-      float* out = part + k * 16;
-      switch (g.rps) {
-        case 16: gemv_rows<16>(st, xc, len, out); break;
-        case 8: gemv_rows<8>(st, xc, len, out); break;
-        case 4: gemv_rows<4>(st, xc, len, out); break;
-        case 2: gemv_rows<2>(st, xc, len, out); break;
-        default: gemv_rows<1>(st, xc, len, out); break;
-      }
-      release_owned(gi);
-    }
-    ring.g += ns;
+    const int nblk = ns / ((16 / g.rps) * g.chunks);
+    const uint32_t timing = (p.record && p.timings) ? (uint32_t)(qidx * p.Q + iidx) : 0xffffffffu;
+    const uint2 r = gemv_blocks(p, ring.stages, ring.full, ring.empty, ring.g, broken, act, nblk, S, x_base, part,
+                                timing, iidx);
+    ring.g = r.x;
+    broken = r.y != 0;
     sync();
   }
 
@@ -265,13 +315,13 @@ struct Consumer {
     return reinterpret_cast<float*>(act + ((K * 2 + 15) & ~15));
   }
 
-  // Row r of the 16-row block whose stages start at part[first * 16] (fixed
-  // summation order over the row's column chunks).
+  // Row r of the 16-row block whose stages start at stage `first` (warps in
+  // order).
   __device__ __forceinline__ static float row_sum(const float* part, int first, int S, int r) {
-    const GemvShape g = gemv_shape(S);
-    const int rg = r / g.rps, i = r % g.rps;
+    const float* ps = part + (size_t)(first / stages_per_row_block(S)) * BLOCK_PART + r * CW;
     float v = 0.f;
-    for (int c = 0; c < g.chunks; ++c) v += part[(first + rg * g.chunks + c) * 16 + i];
+#pragma unroll
+    for (int w = 0; w < CW; ++w) v += ps[w];
     return v;
   }
 
@@ -334,72 +384,81 @@ struct Consumer {
     }
   }
 
-  // Attention keeps one lane group per token: a warp holds TPW tokens of a
-  // ring stage, LPT = 32 / TPW lanes per token, 16 head dims per lane. Scores
-  // need a LPT-lane reduction, and the online-softmax update runs once per
-  // tile of TPW tokens (warp-wide max / sum), not once per token.
-  __device__ __forceinline__ static void load16(const __nv_bfloat16* src, float* out, bool global) {
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4 a, b;
-    if (global) {
-      a = __ldcg(s4);
-      b = __ldcg(s4 + 1);
-    } else {
-      a = s4[0];
-      b = s4[1];
-    }
-    const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      out[2 * k] = bf_lo(u[k]);
-      out[2 * k + 1] = bf_hi(u[k]);
-    }
-  }
+  // Attention over a ring stage of TK tokens (K rows at st, V rows at
+  // st + HALF_STAGE, D bf16 each): warp w takes tokens [w * TPW, w * TPW + TPW).
+  // Lanes have two roles per tile.
+  // - score role: lane = (token * MAX_GQA + head) * LPP + half computes the
+  //   q . k dot over D / LPP dims, q held in registers as bf16 (qr). Chunks are
+  //   read in an order rotated by (token * LPP + half) so that the lanes of a
+  //   warp hit distinct shared-memory banks; qr is stored in the same rotation.
+  // - output role: lane = group * MAX_GQA + head accumulates VD = D / 8 output
+  //   dims [group * VD, group * VD + VD) of its head; its token weights come
+  //   from the score lanes by shuffles.
+  // The warp keeps an online softmax per head over its own tokens (one max and
+  // one sum reduction per tile); warps are merged at the end.
+  template <int D>
+  struct AttnRoles {
+    static constexpr int TK = HALF_STAGE / (D * 2);   // tokens per stage
+    static constexpr int TPW = TK / CW;               // tokens per warp per stage
+    static constexpr int LPP = 32 / (TPW * MAX_GQA);  // lanes per (token, head)
+    static constexpr int DPL = D / LPP;               // dims per score lane
+    static constexpr int NQ = DPL / 8;                // 16-byte chunks per score lane
+    static constexpr int VD = MAX_GQA * D / 32;       // output dims per lane
+    static_assert(LPP >= 1 && LPP * TPW * MAX_GQA == 32, "lane roles");
+  };
 
-  // One tile: this lane's token row (k, v point at the lane's 16 dims), `valid`
-  // per lane group. All 32 lanes must call it.
-  template <int LPT>
-  __device__ __forceinline__ void attend_tile(const float* q,
-                                              float (&acc)[MAX_GQA][16], float* m, float* l,
-                                              const __nv_bfloat16* k, const __nv_bfloat16* v,
-                                              bool valid, bool global, int gqa) {
-    float kv[16], vv[16];
-    if (valid) {
-      load16(k, kv, global);
-      load16(v, vv, global);
-    } else {
+  template <int D>
+  __device__ __forceinline__ void attend_tile(const uint8_t* kb, const uint8_t* vb, int nvalid, bool global,
+                                              const uint4 (&qr)[AttnRoles<D>::NQ], float& ms, float& ls,
+                                              float (&acc)[AttnRoles<D>::VD], int gqa) {
+    using R = AttnRoles<D>;
+    const int pair = lane / R::LPP, half = lane % R::LPP;
+    const int stok = pair / MAX_GQA, sh = pair % MAX_GQA;
+    const int oh = lane % MAX_GQA, od0 = (lane / MAX_GQA) * R::VD;
+    const bool sv = stok < nvalid && sh < gqa;
+    float d = 0.f;
+    if (sv) {
+      const int rot = stok * R::LPP + half;
+      const uint4* k4 = reinterpret_cast<const uint4*>(kb + (size_t)stok * D * 2 + half * R::DPL * 2);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) kv[e] = vv[e] = 0.f;
+      for (int i = 0; i < R::NQ; ++i) {
+        const int c = (i + rot) % R::NQ;
+        const uint4 w = global ? __ldcg(k4 + c) : k4[c];
+        d = dot8_bf16(w, qr[i], d);
+      }
     }
 #pragma unroll
-    for (int h = 0; h < MAX_GQA; ++h) {
-      if (h >= gqa) break;
-      float d = 0.f;
+    for (int o = 1; o < R::LPP; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    const float sc = sv ? d * p.scale : -INFINITY;
+    float mt = sc;
 #pragma unroll
-      for (int e = 0; e < 16; e += 4) {
-        const float4 qq = *reinterpret_cast<const float4*>(q + h * 128 + e);
-        d = fmaf(qq.x, kv[e], d);
-        d = fmaf(qq.y, kv[e + 1], d);
-        d = fmaf(qq.z, kv[e + 2], d);
-        d = fmaf(qq.w, kv[e + 3], d);
+    for (int o = MAX_GQA * R::LPP; o < 32; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+    const float mn = fmaxf(ms, mt);
+    const float mref = mn == -INFINITY ? 0.f : mn;
+    const float corr = expf(ms - mref);
+    const float pe = sv ? expf(sc - mref) : 0.f;
+    float ps = pe;
+#pragma unroll
+    for (int o = MAX_GQA * R::LPP; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    ls = ls * corr + ps;
+    ms = mn;
+    // output role: rescale, then add the tile's weighted V rows
+    const float co = __shfl_sync(0xffffffffu, corr, oh * R::LPP);
+#pragma unroll
+    for (int e = 0; e < R::VD; ++e) acc[e] *= co;
+    for (int t = 0; t < nvalid; ++t) {  // warp-uniform bound
+      const float pt = __shfl_sync(0xffffffffu, pe, (t * MAX_GQA + oh) * R::LPP);
+      const uint4* v4 = reinterpret_cast<const uint4*>(vb + (size_t)t * D * 2 + od0 * 2);
+#pragma unroll
+      for (int c = 0; c < R::VD / 8; ++c) {
+        const uint4 v = global ? __ldcg(v4 + c) : v4[c];
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[c * 8 + 2 * q] = fmaf(pt, bf_lo(u[q]), acc[c * 8 + 2 * q]);
+          acc[c * 8 + 2 * q + 1] = fmaf(pt, bf_hi(u[q]), acc[c * 8 + 2 * q + 1]);
+        }
       }
-#pragma unroll
-      for (int o = 1; o < LPT; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-      const float sc = valid ? d * p.scale : -INFINITY;
-      float mt = sc;
-#pragma unroll
-      for (int o = LPT; o < 32; o <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-      const float mn = fmaxf(m[h], mt);
-      const float mref = mn == -INFINITY ? 0.f : mn;
-      const float corr = expf(m[h] - mref);
-      const float pe = valid ? expf(sc - mref) : 0.f;
-      float ps = pe;
-#pragma unroll
-      for (int o = LPT; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-      l[h] = l[h] * corr + ps;
-      m[h] = mn;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) acc[h][e] = fmaf(pe, vv[e], acc[h][e] * corr);
     }
   }
 
@@ -408,10 +467,7 @@ struct Consumer {
   // log2(sum(exp(scores))).
   template <int D>
   __device__ void op_partial(const Ins& ins, const Plan& pl) {
-    constexpr int TK = HALF_STAGE / (D * 2);  // tokens per stage
-    constexpr int TPW = TK / CW;              // tokens per warp per stage
-    constexpr int LPT = 32 / TPW;             // lanes per token
-    static_assert(LPT * 16 == D, "16 dims per lane");
+    using R = AttnRoles<D>;
     const int l = ins.w[1], kvh = ins.w[2], P = ins.w[3], part = ins.w[4];
     const int gqa = p.gqa, hs = kvh * gqa, bph = D / 16;
     {
@@ -425,60 +481,50 @@ struct Consumer {
     }
     stamp(1);
     const TokenRange tr = partial_tokens(p, P, part);
-    const int grp = lane / LPT, sub = lane % LPT;
-    // q of the group's heads, fp32, in shared memory: qs[h * 128 + d]
-    float* qs = reinterpret_cast<float*>(act + 24576);
-    for (int i = tid; i < gqa * D; i += NC)
-      qs[(i / D) * 128 + i % D] = ldcg_bf16(p.q + (size_t)hs * D + i);
-    sync();
-    const float* q = qs + sub * 16;
-    stamp(3);
-    float acc[MAX_GQA][16], m[MAX_GQA], lsum[MAX_GQA];
+    // this lane's q chunks (score role), rotated like the K reads
+    uint4 qr[R::NQ];
+    {
+      const int pair = lane / R::LPP, half = lane % R::LPP;
+      const int stok = pair / MAX_GQA, sh = pair % MAX_GQA;
+      const int rot = stok * R::LPP + half;
+      const uint4* q4 = reinterpret_cast<const uint4*>(p.q + (size_t)(hs + (sh < gqa ? sh : 0)) * D + half * R::DPL);
 #pragma unroll
-    for (int h = 0; h < MAX_GQA; ++h) {
-      m[h] = -INFINITY;
-      lsum[h] = 0.f;
-#pragma unroll
-      for (int e = 0; e < 16; ++e) acc[h][e] = 0.f;
+      for (int i = 0; i < R::NQ; ++i) qr[i] = __ldcg(q4 + (i + rot) % R::NQ);
     }
+    stamp(3);
+    float ms = -INFINITY, ls = 0.f, acc[R::VD];
+#pragma unroll
+    for (int e = 0; e < R::VD; ++e) acc[e] = 0.f;
     for (int k = 0; k < pl.ns; ++k) {
       const uint8_t* st = acquire();
-      const int j = warp * TPW + grp;
-      const bool valid = tr.t_begin + k * TK + j < tr.t_load_end;
-      const __nv_bfloat16* kr = reinterpret_cast<const __nv_bfloat16*>(st + j * D * 2) + sub * 16;
-      const __nv_bfloat16* vr = reinterpret_cast<const __nv_bfloat16*>(st + HALF_STAGE + j * D * 2) + sub * 16;
-      attend_tile<LPT>(q, acc, m, lsum, kr, vr, valid, false, gqa);
+      const int t0 = tr.t_begin + k * R::TK + warp * R::TPW;
+      const int nvalid = max(0, min(R::TPW, tr.t_load_end - t0));
+      if (nvalid > 0)
+        attend_tile<D>(st + (size_t)warp * R::TPW * D * 2, st + HALF_STAGE + (size_t)warp * R::TPW * D * 2,
+                       nvalid, false, qr, ms, ls, acc, gqa);
       release();
     }
     // the token appended by this step's QKV instructions is read from global
     if (warp == 0 && p.pos >= tr.t_begin && p.pos < tr.t_end) {
-      const size_t off = ((size_t)l * p.T + p.pos) * (p.Hkv * D) + (size_t)kvh * D + sub * 16;
-      attend_tile<LPT>(q, acc, m, lsum, p.k_cache + off, p.v_cache + off, grp == 0, true, gqa);
+      const size_t off = (((size_t)l * p.T + p.pos) * p.Hkv + kvh) * D;
+      attend_tile<D>(reinterpret_cast<const uint8_t*>(p.k_cache + off),
+                     reinterpret_cast<const uint8_t*>(p.v_cache + off), 1, true, qr, ms, ls, acc, gqa);
     }
     stamp(4);
-    // sum each lane's V accumulator over the warp's token groups
-#pragma unroll
-    for (int h = 0; h < MAX_GQA; ++h) {
-      if (h >= gqa) break;
-#pragma unroll
-      for (int e = 0; e < 16; ++e)
-#pragma unroll
-        for (int o = LPT; o < 32; o <<= 1) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
-    }
     // merge the per-warp online-softmax states
     float* mm = reinterpret_cast<float*>(act);  // [CW][gqa]
     float* ll = mm + CW * MAX_GQA;              // [CW][gqa]
     float* aa = ll + CW * MAX_GQA;              // [CW][gqa][D]
-#pragma unroll
-    for (int h = 0; h < MAX_GQA; ++h) {
-      if (h >= gqa) break;
-      if (lane == 0) {
-        mm[warp * gqa + h] = m[h];
-        ll[warp * gqa + h] = lsum[h];
+    {
+      const int oh = lane % MAX_GQA, od0 = (lane / MAX_GQA) * R::VD;
+      // score lanes of token 0 hold each head's state
+      if (lane < MAX_GQA * R::LPP && lane % R::LPP == 0 && lane / R::LPP < gqa) {
+        mm[warp * gqa + lane / R::LPP] = ms;
+        ll[warp * gqa + lane / R::LPP] = ls;
       }
-      if (grp == 0) {
+      if (oh < gqa) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) aa[(warp * gqa + h) * D + sub * 16 + e] = acc[h][e];
+        for (int e = 0; e < R::VD; ++e) aa[(warp * gqa + oh) * D + od0 + e] = acc[e];
       }
     }
     sync();
@@ -884,7 +930,7 @@ struct Consumer {
     float* part = partials_after(p.I);
     for (int es = 0; es < p.topk; ++es) {
       copy_to_act(p.expert_silu + (size_t)rsel[es] * p.I, p.I);
-      gemv_stream(nse, p.I, part + es * nse * 16);
+      gemv_stream(nse, p.I, part + es * nb * BLOCK_PART);
     }
     stamp(4);
     if (p.tp_world > 1) {
@@ -892,7 +938,7 @@ struct Consumer {
       for (int idx = tid; idx < p.topk * nb * 16; idx += NC) {
         const int es = idx / (nb * 16), j = (idx / 16) % nb, r = idx % 16;
         const int row = (b0 + j) * 16 + r;
-        const float v = row_sum(part + es * nse * 16, j * spb, p.I, r);
+        const float v = row_sum(part + es * nb * BLOCK_PART, j * spb, p.I, r);
         for (int rk = 0; rk < p.tp_world; ++rk)
           tp_slot(rk, p.tp_off_recv_d)[((size_t)p.tp_rank * p.topk + es) * p.H + row] = v;
       }
@@ -915,7 +961,7 @@ struct Consumer {
       const int row = (b0 + j) * 16 + r;
       float h = ldcg_bf16(p.hidden + row);
       for (int es = 0; es < p.topk; ++es) {
-        const float v = bf16r(row_sum(part + es * nse * 16, j * spb, p.I, r));
+        const float v = bf16r(row_sum(part + es * nb * BLOCK_PART, j * spb, p.I, r));
         h = bf16r(h + bf16r(rscore[es] * v));
       }
       p.hidden[row] = __float2bfloat16_rn(h);
@@ -1054,6 +1100,34 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
     }
     wk.init(p, ins, pl, ex);
     while (!wk.done()) {
+      const uint8_t* src;
+      uint32_t bytes;
+      const int run = wk.contiguous_run(p, src, bytes);
+      if (run > 0) {  // fast path: consecutive whole-row stages
+        for (int t = 0; t < run; ++t) {
+          uint64_t* empty = &ring.empty[ring.slot];
+          const uint32_t parity = ring.phase ^ 1u;
+          if (!mbar_test_wait(empty, parity)) {
+            bool more = p.pf_stages > 0;
+            while (more && pf.g < g_load + p.pf_stages && !mbar_test_wait(empty, parity))
+              more = pf.step(p, q, g_load);
+            if (!ring_wait(empty, parity, ring_timeout)) {
+              record_error(p, 4, i, pl.op, pl.layer, ring.slot, (int)ring.phase, -1);
+              return;
+            }
+          }
+          if (p.record && p.timings && wk.k + t < 56)
+            p.timings[((size_t)q * p.Q + i) * 128 + 64 + wk.k + t] = (int)(globaltimer() & 0x7fffffff);
+          uint64_t* fb = &ring.full[ring.slot];
+          mbar_arrive_expect_tx(fb, bytes);
+          bulk_load(ring.stages + (size_t)ring.slot * STAGE_BYTES, src, bytes, fb);
+          src += bytes;
+          ring_advance(ring);
+          ++g_load;
+        }
+        wk.skip_run(p, run);
+        continue;
+      }
       uint64_t* empty = &ring.empty[ring.slot];
       const uint32_t parity = ring.phase ^ 1u;
       if (!mbar_test_wait(empty, parity)) {
@@ -1066,6 +1140,8 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
           return;
         }
       }
+      if (p.record && p.timings && wk.k < 56)
+        p.timings[((size_t)q * p.Q + i) * 128 + 64 + wk.k] = (int)(globaltimer() & 0x7fffffff);
       wk.issue<false>(p, ring.stages + (size_t)ring.slot * STAGE_BYTES, &ring.full[ring.slot]);
       ring_advance(ring);
       ++g_load;

@@ -41,14 +41,14 @@ constexpr int NTHREADS = NC + 32;     // + loader warp
 constexpr int STAGE_BYTES = 16384;    // one ring stage
 constexpr int HALF_STAGE = 8192;      // one TMA box (16 rows x 256 bf16, or TK x D bf16)
 constexpr int ACT_BYTES = 49152;      // activation vector + per-stage partial sums / attention merge
-// Ring slots. Must be a multiple of CW: GEMV stage g is owned by warp g % CW
-// and sits in slot g % NUM_STAGES, so every slot always belongs to the same
-// warp, which visits its laps in order. (With other sizes a fast owner can wait
-// on a slot two laps ahead, where an mbarrier parity wait is ambiguous.)
+// Ring slots. Every consumer warp reads every stage in stream order (the
+// GEMVs split a stage's pieces over all warps), so a warp waiting on a slot is
+// never more than one lap ahead of it and any slot count works. 8 slots keep
+// the shared-memory carve-out small enough to leave L1 for the threads' stacks.
 constexpr int NUM_STAGES = 8;         // 128 KiB ring
 constexpr int CTRL_BYTES = 1024;      // mbarriers + reduction scratch
 constexpr int SMEM_BYTES = NUM_STAGES * STAGE_BYTES + ACT_BYTES + CTRL_BYTES;
-static_assert(NUM_STAGES % CW == 0, "ring slots must map to a fixed owner warp");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 constexpr int MAX_GQA = 4;  // query heads per KV head
 constexpr int MAX_EXPERTS = 16;
 constexpr int MAX_TOPK = 4;
@@ -187,10 +187,13 @@ __device__ __forceinline__ int stages_per_row_block(int S) {
   return (16 / g.rps) * g.chunks;
 }
 
+// Floats of partial row sums one 16-row GEMV block leaves: 16 rows x CW warps.
+constexpr int BLOCK_PART = 16 * CW;
+
 // Bytes of `act` a GEMV instruction needs: its activation slice (K bf16) and
-// one 16-float partial row per ring stage.
-__device__ __forceinline__ int gemv_act_bytes(int K, int ns) {
-  return ((K * 2 + 15) & ~15) + ns * 64;
+// the partial sums of its ns ring stages of S-column row segments.
+__device__ __forceinline__ int gemv_act_bytes(int K, int ns, int S = -1) {
+  return ((K * 2 + 15) & ~15) + (ns / stages_per_row_block(S < 0 ? K : S)) * BLOCK_PART * 4;
 }
 
 // Token range [t_begin, t_end) of one partial (python_vm.py:306-318), and the
@@ -260,7 +263,7 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
         if (w[2] > p.V / 16) { bad(2); break; }
         if (w[3] < 0 || (w[3] + 1) * LM_HEAD_SPLIT > p.H) { bad(3); break; }
         pl.ns = (w[2] - w[1]) * stages_per_row_block(LM_HEAD_SPLIT);
-        if (gemv_act_bytes(p.H, pl.ns) > ACT_BYTES) { bad(2); break; }
+        if (gemv_act_bytes(p.H, pl.ns, LM_HEAD_SPLIT) > ACT_BYTES) { bad(2); break; }
         break;
       }
       case OP_PREDICT: {  // SpeculativeExpertPredict: layer
@@ -506,6 +509,47 @@ struct StageWalker {
     }
     advance(p);
     return bytes;
+  }
+
+  // Fast path: the number of stages from here on that are whole-row copies
+  // from one contiguous source, each `bytes` long and following the previous
+  // one in memory (0 if the current stage needs the general path). Sets
+  // src/bytes; the run's bounds are checked here, once.
+  __device__ __forceinline__ int contiguous_run(const KParams& p, const uint8_t*& src, uint32_t& bytes) {
+    if (op == OP_PARTIAL || chunks != 1 || S != stride || col0 != 0) return 0;
+    int n = groups - rg;
+    if (nmat == 1) n = (int)min((long long)(ns - k), (long long)(nblocks - j) * groups - rg);
+    const long long row = row_base + (long long)rg * rps;
+    bytes = (uint32_t)(rps * S * 2);
+    src = reinterpret_cast<const uint8_t*>(mat[m] + row * stride);
+    if (n < 1 || row < 0 || row + (long long)n * rps > mat_rows || bytes > (uint32_t)STAGE_BYTES ||
+        ((reinterpret_cast<uintptr_t>(src) | bytes) & 15u))
+      return 0;  // the general path checks (and reports) each stage
+    return n;
+  }
+
+  // Advance over a run of n stages returned by contiguous_run.
+  __device__ __forceinline__ void skip_run(const KParams& p, int n) {
+    k += n;
+    if (nmat == 1) {
+      rg += n;
+      j += rg / groups;
+      rg %= groups;
+      if (j == nblocks) {  // Mixtral expert ops: next selected expert
+        j = 0;
+        ++es;
+      }
+    } else {
+      rg = 0;
+      if (++m == nmat) {
+        m = 0;
+        if (++j == nblocks) {
+          j = 0;
+          ++es;
+        }
+      }
+    }
+    if (k < ns) row_base = block_row(p, j);
   }
 
   // Move to the next stage without issuing anything.

@@ -180,6 +180,21 @@ __device__ __forceinline__ float ldcg_bf16(const __nv_bfloat16* p) {
   return __uint_as_float(static_cast<uint32_t>(u) << 16);
 }
 
+// a + sum_i w[i] * x[i] over the 8 bf16 pairs of two 16-byte pieces, one
+// rounding per step in order i = 0..7 (fma with bf16 inputs and an fp32
+// accumulator; a bf16 x bf16 product is exact in fp32, so each step equals
+// fmaf(float(w[i]), float(x[i]), a)).
+__device__ __forceinline__ float dot8_bf16(const uint4& w, const uint4& x, float a) {
+  asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+      "mov.b32 {w0, w1}, %1; mov.b32 {x0, x1}, %5; fma.rn.f32.bf16 %0, w0, x0, %0; fma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+      "mov.b32 {w0, w1}, %2; mov.b32 {x0, x1}, %6; fma.rn.f32.bf16 %0, w0, x0, %0; fma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+      "mov.b32 {w0, w1}, %3; mov.b32 {x0, x1}, %7; fma.rn.f32.bf16 %0, w0, x0, %0; fma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+      "mov.b32 {w0, w1}, %4; mov.b32 {x0, x1}, %8; fma.rn.f32.bf16 %0, w0, x0, %0; fma.rn.f32.bf16 %0, w1, x1, %0;\n\t}"
+      : "+f"(a)
+      : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+  return a;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
