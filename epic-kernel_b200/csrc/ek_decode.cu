@@ -1100,10 +1100,9 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
     }
     wk.init(p, ins, pl, ex);
     while (!wk.done()) {
-      const uint8_t* src;
-      uint32_t bytes;
-      const int run = wk.contiguous_run(p, src, bytes);
-      if (run > 0) {  // fast path: consecutive whole-row stages
+      StageWalker::Run rr;
+      const int run = wk.contiguous_run(p, rr);
+      if (run > 0) {  // fast path: stages at a fixed stride
         for (int t = 0; t < run; ++t) {
           uint64_t* empty = &ring.empty[ring.slot];
           const uint32_t parity = ring.phase ^ 1u;
@@ -1119,9 +1118,10 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
           if (p.record && p.timings && wk.k + t < 56)
             p.timings[((size_t)q * p.Q + i) * 128 + 64 + wk.k + t] = (int)(globaltimer() & 0x7fffffff);
           uint64_t* fb = &ring.full[ring.slot];
-          mbar_arrive_expect_tx(fb, bytes);
-          bulk_load(ring.stages + (size_t)ring.slot * STAGE_BYTES, src, bytes, fb);
-          src += bytes;
+          uint8_t* dst = ring.stages + (size_t)ring.slot * STAGE_BYTES;
+          mbar_arrive_expect_tx(fb, rr.bytes * (uint32_t)rr.copies);
+          for (int c = 0; c < rr.copies; ++c) bulk_load(dst + c * rr.bytes, rr.src + c * rr.row_step, rr.bytes, fb);
+          rr.src += rr.stage_step;
           ring_advance(ring);
           ++g_load;
         }

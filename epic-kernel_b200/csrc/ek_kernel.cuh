@@ -511,19 +511,32 @@ struct StageWalker {
     return bytes;
   }
 
-  // Fast path: the number of stages from here on that are whole-row copies
-  // from one contiguous source, each `bytes` long and following the previous
-  // one in memory (0 if the current stage needs the general path). Sets
-  // src/bytes; the run's bounds are checked here, once.
-  __device__ __forceinline__ int contiguous_run(const KParams& p, const uint8_t*& src, uint32_t& bytes) {
-    if (op == OP_PARTIAL || chunks != 1 || S != stride || col0 != 0) return 0;
+  // Fast path: the number of stages from here on that follow each other at a
+  // fixed stride in one matrix: a stage is `copies` copies of `bytes` each,
+  // copy c at src + c * row_step, and the next stage starts stage_step bytes
+  // further (one copy per stage for whole rows, one per row for row segments
+  // of a column split). 0 if the current stage needs the general path. The
+  // run's bounds and alignment are checked here, once.
+  struct Run {
+    const uint8_t* src;
+    uint32_t bytes;
+    int copies;
+    long long row_step, stage_step;
+  };
+  __device__ __forceinline__ int contiguous_run(const KParams& p, Run& r) {
+    if (op == OP_PARTIAL || chunks != 1) return 0;
     int n = groups - rg;
     if (nmat == 1) n = (int)min((long long)(ns - k), (long long)(nblocks - j) * groups - rg);
     const long long row = row_base + (long long)rg * rps;
-    bytes = (uint32_t)(rps * S * 2);
-    src = reinterpret_cast<const uint8_t*>(mat[m] + row * stride);
-    if (n < 1 || row < 0 || row + (long long)n * rps > mat_rows || bytes > (uint32_t)STAGE_BYTES ||
-        ((reinterpret_cast<uintptr_t>(src) | bytes) & 15u))
+    const bool whole = S == stride && col0 == 0;
+    r.copies = whole ? 1 : rps;
+    r.bytes = (uint32_t)(whole ? rps * S * 2 : S * 2);
+    r.row_step = (long long)stride * 2;
+    r.stage_step = (long long)rps * stride * 2;
+    r.src = reinterpret_cast<const uint8_t*>(mat[m] + row * stride + col0);
+    if (n < 1 || row < 0 || row + (long long)n * rps > mat_rows || col0 < 0 || col0 + S > stride ||
+        (uint32_t)r.copies * r.bytes > (uint32_t)STAGE_BYTES ||
+        ((reinterpret_cast<uintptr_t>(r.src) | r.bytes | (uint32_t)r.row_step) & 15u))
       return 0;  // the general path checks (and reports) each stage
     return n;
   }
