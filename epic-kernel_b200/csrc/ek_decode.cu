@@ -1038,7 +1038,7 @@ struct PrefetchCursor {
   bool have = false;
   long long g = 0;  // stream index of the walker's current stage
   int issued = 0;   // prefetched stages (diagnostics)
-  Ins ins;
+  Ins* ins = nullptr;  // its instruction words (shared memory)
   StageWalker wk;
 
   // Prefetch (or skip, if already loaded) one stage; false when exhausted.
@@ -1046,13 +1046,13 @@ struct PrefetchCursor {
     while (true) {
       if (!have) {
         if (i >= p.Q) return false;
-        fetch_ins(p, q, i, ins);
+        fetch_ins(p, q, i, *ins);
         // Mixtral expert instructions: the predicted experts (a hint written
         // by SpeculativeExpertPredict; stale values only cost a wasted prefetch)
         int pred[MAX_TOPK] = {0, 0, 0, 0};
         if (p.model == MODEL_MIXTRAL)
           for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) pred[t] = ld_relaxed(p.pred_idx + t);
-        wk.init(p, ins, make_plan(p, ins), pred);
+        wk.init(p, *ins, make_plan(p, *ins), pred);
         have = true;
       }
       if (wk.done()) {
@@ -1072,11 +1072,15 @@ struct PrefetchCursor {
   }
 };
 
-__device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_t* mbox_bar) {
+// lins / pins: shared-memory instruction buffers of the loader and of its L2
+// prefetch cursor (dynamically indexed words stay out of local memory).
+__device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_t* mbox_bar, Ins* lins,
+                           Ins* pins) {
   const int q = blockIdx.x;
-  Ins ins;
+  Ins& ins = *lins;
   StageWalker wk;
   PrefetchCursor pf;
+  pf.ins = pins;
   long long g_load = 0;
   uint32_t mbox_phase = 0;
   const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
@@ -1169,6 +1173,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   float* rlog = reinterpret_cast<float*>(mbox + MAX_TOPK);  // MAX_EXPERTS
   int* rsel = reinterpret_cast<int*>(rlog + MAX_EXPERTS);   // MAX_TOPK
   float* rscore = reinterpret_cast<float*>(rsel + MAX_TOPK);  // MAX_TOPK
+  // instruction words: consumers, loader, loader's prefetch cursor
+  Ins* ins_smem = reinterpret_cast<Ins*>(act + ACT_BYTES + 512);
+  static_assert(512 + 3 * sizeof(Ins) <= CTRL_BYTES, "control area");
 
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   if (tid == 0) {
@@ -1187,7 +1194,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
 
   Ring ring{stages, full, empty, 0, 0u, 0u};
   if (warp == CW) {
-    if (lane == 0) run_loader(p, ring, mbox, mbox_bar);
+    if (lane == 0) run_loader(p, ring, mbox, mbox_bar, ins_smem + 1, ins_smem + 2);
     return;
   }
 
@@ -1207,16 +1214,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   c.qidx = blockIdx.x;
   c.broken = false;
 
-  Ins ins;
+  Ins& ins = ins_smem[0];
   for (int i = 0; i < p.Q; ++i) {
     c.iidx = i;
-    fetch_ins(p, blockIdx.x, i, ins);
+    // every consumer finished the previous instruction (trailing barrier)
+    if (tid < 32) ins.w[tid] = __ldg(p.instructions + ((size_t)blockIdx.x * p.Q + i) * 32 + tid);
+    c.sync();
     const Plan pl = make_plan(p, ins);
     c.stamp(0);
     if (pl.bad_word >= 0) {
       if (tid == 0)
         record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > (p.model == MODEL_MIXTRAL ? OP_PREDICT : OP_LM_HEAD)) ? 2 : 3, i, pl.op,
                      pl.layer, 0, pl.bad_word, ins.w[pl.bad_word]);
+      c.sync();  // before the next instruction's words overwrite these
       continue;  // no stages were planned for it
     }
     if (p.model == MODEL_MIXTRAL && pl.op >= OP_UPGATE) {
