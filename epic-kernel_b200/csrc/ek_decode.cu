@@ -1072,6 +1072,38 @@ struct PrefetchCursor {
   }
 };
 
+// L2-prefetch the weights of instruction i of queue q: one bulk prefetch per
+// contiguous run (per row segment for strided runs), the general walker for
+// the rest. KV stages are not prefetched (the partial's range is small and its
+// newest rows are written during the step). Mixtral expert instructions use
+// the predicted experts (a hint; a wrong guess only wastes the prefetch).
+__device__ void prefetch_instruction(const KParams& p, int q, int i, Ins* ins) {
+  if (i >= p.Q) return;
+  fetch_ins(p, q, i, *ins);
+  const Plan pl = make_plan(p, *ins);
+  if (pl.bad_word >= 0 || pl.ns == 0 || pl.op == OP_PARTIAL) return;
+  int pred[MAX_TOPK] = {0, 0, 0, 0};
+  if (p.model == MODEL_MIXTRAL)
+    for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) pred[t] = ld_relaxed(p.pred_idx + t);
+  StageWalker w;
+  w.init(p, *ins, pl, pred);
+  while (!w.done()) {
+    StageWalker::Run r;
+    const int n = w.contiguous_run(p, r);
+    if (n > 0) {
+      if (r.copies == 1 && r.stage_step == (long long)r.bytes) {
+        bulk_prefetch_l2(r.src, r.bytes * (uint32_t)n);
+      } else {
+        for (int t = 0; t < n; ++t)
+          for (int c = 0; c < r.copies; ++c) bulk_prefetch_l2(r.src + t * r.stage_step + c * r.row_step, r.bytes);
+      }
+      w.skip_run(p, n);
+    } else {
+      w.issue<true>(p, nullptr, nullptr);
+    }
+  }
+}
+
 // lins / pins: shared-memory instruction buffers of the loader and of its L2
 // prefetch cursor (dynamically indexed words stay out of local memory).
 __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_t* mbox_bar, Ins* lins,
@@ -1103,6 +1135,7 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
       for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) ex[t] = mbox[t];
     }
     wk.init(p, ins, pl, ex);
+    if (p.pf_next) prefetch_instruction(p, q, i + 1, pins);
     while (!wk.done()) {
       StageWalker::Run rr;
       const int run = wk.contiguous_run(p, rr);

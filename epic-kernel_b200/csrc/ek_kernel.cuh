@@ -137,6 +137,7 @@ struct KParams {
   float scale, eps;
   int down_R, o_R, down_splits, o_splits;
   int pf_stages, record;
+  int pf_next;  // L2-prefetch the next instruction's weights when an instruction starts loading
   long long timeout_ns;
   unsigned epoch;
 };

@@ -10,8 +10,11 @@ module serves every Llama size, because the model dimensions are read from the
 tensor shapes instead of being compiled in.
 
 Extra keyword-only options (defaults match the reference's behaviour):
-  l2_prefetch_stages  16 KiB weight stages prefetched into L2 ahead of the
-                      shared-memory ring (0 = off)
+  l2_prefetch_stages  > 0: 16 KiB weight stages prefetched into L2 ahead of
+                      the shared-memory ring while it is full; < 0: the next
+                      instruction's whole weight range prefetched into L2
+                      when an instruction starts loading; 0 = off (default;
+                      both modes measured slower on B200)
   timeout_ns          bound of every cross-SM wait (default 1 s)
   record_timings      write start / dependency-ready / end stamps (ns) into
                       timings[q, i, 0..2]

@@ -99,7 +99,8 @@ typedef struct EkLlamaArgs {
 
   int32_t down_reduction_size;  /* columns of W_down per DownProjResidual split (gcd(I, H)) */
   int32_t oproj_reduction_size; /* columns of W_o per O_ProjResidual split (H) */
-  int32_t l2_prefetch_stages;   /* 16 KiB weight stages prefetched into L2 beyond the ring; 0 = off */
+  int32_t l2_prefetch_stages;   /* >0: stages prefetched into L2 beyond the ring; <0: next instruction's
+                                   weights prefetched into L2; 0 = off */
   int32_t record_timings;       /* write timings[q, i, 0..2] when timings != NULL */
   int64_t timeout_ns;           /* bound of every cross-SM wait; <= 0 selects 1 s */
 } EkLlamaArgs;
@@ -150,7 +151,8 @@ typedef struct EkMixtralArgs {
   float rms_norm_eps;
   int32_t skip_attn_reduction;
 
-  int32_t l2_prefetch_stages;   /* lookahead L2 prefetch (also speculative expert prefetch); 0 = off */
+  int32_t l2_prefetch_stages;   /* >0: lookahead L2 prefetch by stages (also speculative expert prefetch);
+                                   <0: next instruction's weights; 0 = off */
   int32_t record_timings;
   int64_t timeout_ns;
 
