@@ -368,7 +368,7 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   p.model = ek::MODEL_LLAMA;
   p.down_done_target = (I / dR) * (H / 16);
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
-  p.pf_next = a->l2_prefetch_stages < 0 ? 1 : 0;
+  p.pf_next = a->l2_prefetch_stages < 0 ? min(-a->l2_prefetch_stages, 2) : 0;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
   if (++ctx->epoch == 0) ctx->epoch = 1;
@@ -603,7 +603,7 @@ extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* s
     p.tp_step = ++ctx->tp_step;
   }
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
-  p.pf_next = a->l2_prefetch_stages < 0 ? 1 : 0;
+  p.pf_next = a->l2_prefetch_stages < 0 ? min(-a->l2_prefetch_stages, 2) : 0;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
   if (++ctx->epoch == 0) ctx->epoch = 1;

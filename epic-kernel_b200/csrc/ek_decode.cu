@@ -1113,6 +1113,7 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
   StageWalker wk;
   PrefetchCursor pf;
   pf.ins = pins;
+  int pf_layer = -1;  // layer whose MLP weights were last prefetched (pf_next == 2)
   long long g_load = 0;
   uint32_t mbox_phase = 0;
   const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
@@ -1135,7 +1136,17 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
       for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) ex[t] = mbox[t];
     }
     wk.init(p, ins, pl, ex);
-    if (p.pf_next) prefetch_instruction(p, q, i + 1, pins);
+    if (p.pf_next == 1) {
+      prefetch_instruction(p, q, i + 1, pins);
+    } else if (p.pf_next == 2 && pl.op >= OP_QKV && pl.op <= OP_OPROJ && pl.layer != pf_layer) {
+      pf_layer = pl.layer;
+      for (int j = i + 1; j < p.Q; ++j) {
+        const int* wj = p.instructions + ((size_t)q * p.Q + j) * 32;
+        const int opj = __ldg(wj), lj = __ldg(wj + 1);
+        if (opj == OP_QKV && lj != pl.layer) break;
+        if ((opj == OP_UPGATE || opj == OP_DOWN) && lj == pl.layer) prefetch_instruction(p, q, j, pins);
+      }
+    }
     while (!wk.done()) {
       StageWalker::Run rr;
       const int run = wk.contiguous_run(p, rr);

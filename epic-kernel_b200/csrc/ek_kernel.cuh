@@ -137,7 +137,11 @@ struct KParams {
   float scale, eps;
   int down_R, o_R, down_splits, o_splits;
   int pf_stages, record;
-  int pf_next;  // L2-prefetch the next instruction's weights when an instruction starts loading
+  // L2 prefetch at instruction granularity (off by default: both measured
+  // slower): 1 = the next instruction's weights when an instruction starts
+  // loading; 2 = this queue's up/gate and down weights of a layer when its
+  // first attention-chain instruction (opcodes 1-4) starts loading.
+  int pf_next;
   long long timeout_ns;
   unsigned epoch;
 };

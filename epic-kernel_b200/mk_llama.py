@@ -11,10 +11,11 @@ tensor shapes instead of being compiled in.
 
 Extra keyword-only options (defaults match the reference's behaviour):
   l2_prefetch_stages  > 0: 16 KiB weight stages prefetched into L2 ahead of
-                      the shared-memory ring while it is full; < 0: the next
+                      the shared-memory ring while it is full; -1: the next
                       instruction's whole weight range prefetched into L2
-                      when an instruction starts loading; 0 = off (default;
-                      both modes measured slower on B200)
+                      when an instruction starts loading; -2: a layer's MLP
+                      weights prefetched when its attention chain starts;
+                      0 = off (default; every mode measured slower on B200)
   timeout_ns          bound of every cross-SM wait (default 1 s)
   record_timings      write start / dependency-ready / end stamps (ns) into
                       timings[q, i, 0..2]
