@@ -71,21 +71,6 @@ EncodeTiledFn get_encoder() {
   return fn;
 }
 
-// bf16 tensor map of a row-major [rows, cols] matrix, box 16 rows x 256 cols.
-int encode_matrix(CUtensorMap* m, const void* base, long long rows, long long cols, const char* name) {
-  EncodeTiledFn enc = get_encoder();
-  if (!enc) return fail(EK_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {256, 16};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(EK_E_INVALID, "tensor map for %s failed (CUresult %d)", name, (int)r);
-  return EK_SUCCESS;
-}
-
 // bf16 tensor map of a KV cache [L*T, Hkv, D], box D x 1 head x tk tokens.
 int encode_kv(CUtensorMap* m, const void* base, long long rows, int hkv, int d, int tk,
               const char* name) {
@@ -319,7 +304,7 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   int rc = grow(ctx, nctr, npart);
   if (rc) return rc;
 
-  static KParams p;  // host staging copy; the launch copies it into kernel parameters
+  KParams p;  // per call (thread-safe); the launch copies it into the kernel parameters
   std::memset(&p, 0, sizeof(p));
   const int qkv_rows = (Hq + 2 * Hkv) * D;
   const int tk = ek::HALF_STAGE / (D * 2);
@@ -367,8 +352,14 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   p.down_R = dR; p.o_R = oR; p.down_splits = I / dR; p.o_splits = H / oR;
   p.model = ek::MODEL_LLAMA;
   p.down_done_target = (I / dR) * (H / 16);
+  p.defer_down = (I / dR > 1 && H / oR == 1) ? min(max(a->deferred_down_layers, 0), L - 1) : 0;
+  p.fuse_red = (a->options & EK_OPT_FUSE_ATTENTION_REDUCTION) ? 1 : 0;
+  if (p.fuse_red && p.gqa * a->max_partials > ek::MAX_GQA * 160)
+    return fail(EK_E_UNSUPPORTED, "fused attention reduction: %d heads x %d partials", p.gqa, a->max_partials);
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
   p.pf_next = a->l2_prefetch_stages < 0 ? min(-a->l2_prefetch_stages, 2) : 0;
+  p.pf_mlp = a->cache_flags;
+  p.pf_gap_ns = a->prefetch_gap_ns > 0 ? (unsigned)a->prefetch_gap_ns : 0u;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
   if (++ctx->epoch == 0) ctx->epoch = 1;
@@ -406,15 +397,6 @@ struct StaticScratch {
   unsigned* counters = nullptr;
   __nv_bfloat16* partials = nullptr;
   unsigned epoch = 0;
-  // Mixtral tensor parallelism
-  int tp_world = 1, tp_rank = 0;
-  int tp_layers = 0, tp_hidden = 0, tp_topk = 0, tp_vocab = 0;
-  char* tp_buf = nullptr;
-  size_t tp_bytes = 0;
-  char* tp_peer[ek::MAX_TP] = {};
-  bool tp_connected = false;
-  unsigned tp_step = 0;
-  long long off_recv_o = 0, off_recv_d = 0, off_cnt_o = 0, off_cnt_d = 0, off_cnt_lm = 0, off_logits = 0;
 };
 
 std::mutex g_static_mu;
@@ -533,7 +515,7 @@ extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* s
   int rc = grow(ctx, 1, 1);
   if (rc) return rc;
 
-  static KParams p;
+  KParams p;  // per call (thread-safe)
   std::memset(&p, 0, sizeof(p));
   const int qkv_rows = (Hq + 2 * Hkv) * D;
   const int tk = ek::HALF_STAGE / (D * 2);
@@ -604,6 +586,8 @@ extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* s
   }
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
   p.pf_next = a->l2_prefetch_stages < 0 ? min(-a->l2_prefetch_stages, 2) : 0;
+  p.pf_mlp = a->cache_flags;
+  p.pf_gap_ns = a->prefetch_gap_ns > 0 ? (unsigned)a->prefetch_gap_ns : 0u;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
   if (++ctx->epoch == 0) ctx->epoch = 1;

@@ -1,14 +1,23 @@
-// Llama batch-1 decode megakernel: loader and consumer roles, the opcode
-// bodies, and the host-side launcher (ek_launch_llama).
+// Batch-1 decode megakernel: loader and consumer roles, the opcode bodies,
+// and the host-side launcher of one kernel variant. This file is compiled
+// once per variant (EK_MODEL, EK_PF, and the namespace EK_NS of the kernel and
+// its launcher are set on the command line; see ek_kernel.cuh).
 //
 // Opcode semantics follow megakernels/demos/latency/python_vm.py of
 // epic-kernel (cited per op); see ek_kernel.cuh for the overall design.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "ek_kernel.cuh"
 #include "ek_launch.h"
 
+#ifndef EK_NS
+#define EK_NS llama
+#endif
+
 namespace ek {
+namespace {  // device code of this variant (internal linkage: one copy per variant)
 
 // ------------------------------------------------------------------ GEMV streaming
 // The GEMV inner loop, as free functions taking the ring state by value (so the
@@ -219,8 +228,10 @@ struct Consumer {
           if ((it & 15u) == 15u) {
             if (aborted(p)) { ok = 0; break; }
             if ((long long)(globaltimer() - t0) > p.timeout_ns) {
+              // detail: index into `barriers`, or -1 for a tensor-parallel
+              // counter in a symmetric buffer
               record_error(p, 1, iidx, opcode, layer, v, targets[j],
-                           (int)(addrs[j] - p.barriers));
+                           sys_scope ? -1 : (int)(addrs[j] - p.barriers));
               ok = 0;
               break;
             }
@@ -246,15 +257,82 @@ struct Consumer {
       p.timings[((size_t)qidx * p.Q + iidx) * 128 + slot] = (int)(globaltimer() & 0x7fffffff);
   }
 
+  // Norm weights a thread needs (its pieces c = tid, tid + NC), loaded before
+  // the counter wait so that their latency overlaps it.
+  struct NormWeights {
+    uint4 w[2];
+  };
+  __device__ __forceinline__ NormWeights preload_norm(const __nv_bfloat16* wt, int n) const {
+    NormWeights r;
+    const uint4* w4 = reinterpret_cast<const uint4*>(wt);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) r.w[k] = tid + k * NC < n / 8 ? __ldg(w4 + tid + k * NC) : make_uint4(0, 0, 0, 0);
+    return r;
+  }
+
+  // Deferred down partials of layer `prev_layer` to add to the residual
+  // stream (defer_down), or 0.
+  __device__ __forceinline__ int deferred_splits(int prev_layer) const {
+    return (prev_layer >= 0 && prev_layer < p.defer_down) ? p.down_splits : 0;
+  }
+  __device__ __forceinline__ const __nv_bfloat16* down_partials() const {
+    return p.split_partials + (size_t)p.o_splits * p.H;
+  }
+
+  // 8 residual values at piece c of `x`, plus the nsplit deferred down
+  // partials added in split order (bf16 rounding after each add).
+  __device__ __forceinline__ uint4 residual8(const __nv_bfloat16* x, int c, int nsplit) const {
+    uint4 v = __ldcg(reinterpret_cast<const uint4*>(x) + c);
+    if (nsplit == 0) return v;
+    uint4 parts[8];
+    const uint4* d4 = reinterpret_cast<const uint4*>(down_partials());
+#pragma unroll
+    for (int j = 0; j < 8; ++j) if (j < nsplit) parts[j] = __ldcg(d4 + (size_t)j * (p.H / 8) + c);
+    float h[8];
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { h[2 * k] = bf_lo(u[k]); h[2 * k + 1] = bf_hi(u[k]); }
+    auto add = [&](const uint4& pv) {
+      const uint32_t q[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        h[2 * k] = bf16r(h[2 * k] + bf_lo(q[k]));
+        h[2 * k + 1] = bf16r(h[2 * k + 1] + bf_hi(q[k]));
+      }
+    };
+#pragma unroll
+    for (int j = 0; j < 8; ++j) if (j < nsplit) add(parts[j]);
+    for (int j = 8; j < nsplit; ++j) add(__ldcg(d4 + (size_t)j * (p.H / 8) + c));
+    return make_uint4(pack_bf16x2(h[0], h[1]), pack_bf16x2(h[2], h[3]), pack_bf16x2(h[4], h[5]),
+                      pack_bf16x2(h[6], h[7]));
+  }
+
+  // Residual-stream value of one row: hidden plus the nsplit deferred down
+  // partials, in split order.
+  __device__ __forceinline__ float residual_value(int row, int nsplit) const {
+    float h = ldcg_bf16(p.hidden + row);
+    if (nsplit == 0) return h;
+    const __nv_bfloat16* d = down_partials() + row;
+    float parts[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) if (j < nsplit) parts[j] = ldcg_bf16(d + (size_t)j * p.H);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) if (j < nsplit) h = bf16r(h + parts[j]);
+    for (int j = 8; j < nsplit; ++j) h = bf16r(h + ldcg_bf16(d + (size_t)j * p.H));
+    return h;
+  }
+
   // xs[i] = bf16(w[i] * bf16(x[i] * rsqrt(mean(x^2) + eps))) for the n-vector at
-  // `x` (python_vm.py:50-56). Leaves xs in `act`.
-  __device__ void rmsnorm_to_act(const __nv_bfloat16* x, const __nv_bfloat16* wt, int n) {
+  // `x` (python_vm.py:50-56), x being the residual stream with `nsplit`
+  // deferred down partials added. Leaves xs in `act`.
+  __device__ void rmsnorm_to_act(const __nv_bfloat16* x, const __nv_bfloat16* wt, int n, NormWeights nw,
+                                 int nsplit = 0) {
     uint4* xs4 = reinterpret_cast<uint4*>(act);
-    const uint4* x4 = reinterpret_cast<const uint4*>(x);
     const uint4* w4 = reinterpret_cast<const uint4*>(wt);
     float ss = 0.f;
+#pragma unroll 1
     for (int c = tid; c < n / 8; c += NC) {
-      uint4 v = __ldcg(x4 + c);
+      uint4 v = residual8(x, c, nsplit);
       xs4[c] = v;
       const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -271,9 +349,10 @@ struct Consumer {
 #pragma unroll
     for (int k = 0; k < CW; ++k) tot += red[k];
     const float r = 1.0f / sqrtf(tot / (float)n + p.eps);
-    for (int c = tid; c < n / 8; c += NC) {
+#pragma unroll 1
+    for (int c = tid, k = 0; c < n / 8; c += NC, ++k) {
       const uint4 v = xs4[c];
-      const uint4 g = __ldg(w4 + c);
+      const uint4 g = k == 0 ? nw.w[0] : k == 1 ? nw.w[1] : __ldg(w4 + c);
       const uint32_t u[4] = {v.x, v.y, v.z, v.w};
       const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
       uint32_t o[4];
@@ -329,6 +408,19 @@ struct Consumer {
   // LayerNorm_QKV_MatVecRopeAppend (python_vm.py:182-262).
   __device__ void op_qkv(const Ins& ins, const Plan& pl) {
     const int l = ins.w[1], b0 = ins.w[2], b1 = ins.w[3];
+    const int qdim = p.Hq * p.D, kdim = p.Hkv * p.D;
+    // loads that do not depend on other SMs, issued before the wait
+    const NormWeights nw = preload_norm(p.attn_ln + (size_t)l * p.H, p.H);
+    float2 rc = make_float2(1.f, 0.f), rs = make_float2(0.f, 0.f);
+    {
+      const int idx = tid;  // first rotary pair of this thread (the epilogue's first iteration)
+      const int row = (b0 + idx / 8) * 16 + 2 * (idx % 8);
+      if (idx < (b1 - b0) * 8 && row < qdim + kdim) {
+        const int seg = row % p.D;
+        rc = *reinterpret_cast<const float2*>(p.rope_cos + (size_t)p.pos * p.D + seg);
+        rs = *reinterpret_cast<const float2*>(p.rope_sin + (size_t)p.pos * p.D + seg);
+      }
+    }
     if (l > 0) {
       int* a = bar(l - 1, OP_DOWN - 1, 0);
       const int t = p.down_done_target;
@@ -338,14 +430,14 @@ struct Consumer {
       return;
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.attn_ln + (size_t)l * p.H, p.H);
+    rmsnorm_to_act(p.hidden, p.attn_ln + (size_t)l * p.H, p.H, nw, deferred_splits(l - 1));
     stamp(3);
-    const int qdim = p.Hq * p.D, kdim = p.Hkv * p.D;
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
     stamp(4);
     // one thread per rotary pair (rows 2i, 2i + 1 of a block)
+#pragma unroll 1
     for (int idx = tid; idx < (b1 - b0) * 8; idx += NC) {
       const int j = idx / 8, pr = idx % 8;
       const int row = (b0 + j) * 16 + 2 * pr;
@@ -353,11 +445,13 @@ struct Consumer {
       float v1 = bf16r(row_sum(part, j * spb, p.H, 2 * pr + 1));
       if (row < qdim + kdim) {
         // interleaved RoPE (llama.py:136-174) in fp32, rounded to bf16 on store
-        const int seg = row % p.D;
-        const float* cs = p.rope_cos + (size_t)p.pos * p.D + seg;
-        const float* sn = p.rope_sin + (size_t)p.pos * p.D + seg;
-        const float o0 = __fadd_rn(__fmul_rn(v0, cs[0]), __fmul_rn(-v1, sn[0]));
-        const float o1 = __fadd_rn(__fmul_rn(v1, cs[1]), __fmul_rn(v0, sn[1]));
+        if (idx != tid) {
+          const int seg = row % p.D;
+          rc = *reinterpret_cast<const float2*>(p.rope_cos + (size_t)p.pos * p.D + seg);
+          rs = *reinterpret_cast<const float2*>(p.rope_sin + (size_t)p.pos * p.D + seg);
+        }
+        const float o0 = __fadd_rn(__fmul_rn(v0, rc.x), __fmul_rn(-v1, rs.x));
+        const float o1 = __fadd_rn(__fmul_rn(v1, rc.y), __fmul_rn(v0, rs.y));
         v0 = o0;
         v1 = o1;
       }
@@ -557,31 +651,53 @@ struct Consumer {
       }
     }
     sync();
-    if (tid == 0) {
-      if (p.skip_red) {
-        red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
-      } else {
-        for (int h = 0; h < gqa; ++h) red_release_add(bar(l, OP_PARTIAL - 1, hs + h), 1);
-      }
+    if (p.skip_red) {
+      if (tid == 0) red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
+      return;
     }
+    if (!p.fuse_red) {
+      if (tid == 0)
+        for (int h = 0; h < gqa; ++h) red_release_add(bar(l, OP_PARTIAL - 1, hs + h), 1);
+      return;
+    }
+    // fused reduction: the last partial of this KV head to arrive merges all P
+    // partials (acquire-release on the head's counter orders the other
+    // partials' writes before the merge's reads)
+    if (tid == 0) {
+      for (int h = 1; h < gqa; ++h) red_release_add(bar(l, OP_PARTIAL - 1, hs + h), 1);
+      *flag = atom_add_acq_rel(bar(l, OP_PARTIAL - 1, hs), 1) == P - 1;
+    }
+    sync();
+    const bool last = *flag != 0;
+    sync();
+    if (last) merge_partials(l, hs, P, nullptr, true, 0);
   }
 
   // AttentionReduction (python_vm.py:360-401): exp2-weighted merge of partials.
-  // The partials' LSEs are staged in shared memory first so that every load of
-  // the merge is issued independently.
   __device__ void op_reduction(const Ins& ins) {
+    if (p.fuse_red) return;  // merged by the last partial of each KV head
     const int l = ins.w[1], hs = ins.w[2], P = ins.w[3], terminal = ins.w[4], n = ins.w[5];
-    const int out_slot = ins.w[6 + n];
     {
       int* a = bar(l, OP_PARTIAL - 1, hs);
       if (!wait_counters(1, &a, &P, OP_REDUCTION, l)) return;
     }
     stamp(1);
+    merge_partials(l, hs, n, ins.w + 6, terminal != 0, ins.w[6 + n]);
+  }
+
+  // Merge the n partials list[0..n) (identity when list is null) of the gqa
+  // query heads starting at hs, and bump the layer's reduction counter. The
+  // partials' LSEs are staged in shared memory first so that every load of
+  // the merge is issued independently.
+  __device__ void merge_partials(int l, int hs, int n, const int* list, bool terminal, int out_slot) {
     const int D = p.D, gqa = p.gqa;
-    float* fac = reinterpret_cast<float*>(act);   // [gqa][n] exp2(lse - max)
-    float* den = fac + MAX_GQA * 32;              // [gqa]
-    for (int i = tid; i < gqa * n; i += NC)
-      fac[i] = __ldcg(p.lse + (size_t)(hs + i / n) * p.maxP + ins.w[6 + i % n]);
+    // [gqa][n] exp2(lse - max), n <= 160, past the partials' merge area
+    float* fac = reinterpret_cast<float*>(act + ACT_BYTES - 4096);
+    float* den = fac + MAX_GQA * 160;  // [gqa]
+    for (int i = tid; i < gqa * n; i += NC) {
+      const int h = i / n, j = i - h * n;
+      fac[i] = __ldcg(p.lse + (size_t)(hs + h) * p.maxP + (list ? list[j] : j));
+    }
     sync();
     if (tid < gqa) {
       float M = -INFINITY;
@@ -597,38 +713,42 @@ struct Consumer {
     sync();
     // compute first, write after a barrier: the output slot may be an input
     float res[4];
-    int cnt = 0;
-    for (int idx = tid; idx < gqa * D; idx += NC, ++cnt) {
-      const int h = idx / D, d = idx % D;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int idx = tid + k * NC;
+      res[k] = 0.f;
+      if (idx >= gqa * D) continue;
+      const int h = idx / D, d = idx - h * D;
       const float* o = p.attn_o + (size_t)(hs + h) * p.maxP * D + d;
       float num = 0.f;
+#pragma unroll 1
       for (int j0 = 0; j0 < n; j0 += 8) {
         float vals[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          vals[j] = j0 + j < n ? __ldcg(o + (size_t)ins.w[6 + j0 + j] * D) : 0.f;
+          vals[j] = j0 + j < n ? __ldcg(o + (size_t)(list ? list[j0 + j] : j0 + j) * D) : 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           if (j0 + j < n) num = fmaf(vals[j], fac[h * n + j0 + j], num);
       }
-      res[cnt] = num / den[h];
+      res[k] = num / den[h];
     }
     sync();
-    cnt = 0;
-    for (int idx = tid; idx < gqa * D; idx += NC, ++cnt) {
-      const int h = idx / D, d = idx % D;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int idx = tid + k * NC;
+      if (idx >= gqa * D) continue;
+      const int h = idx / D, d = idx - h * D;
       if (terminal) {
-        p.attn_out[(size_t)(hs + h) * D + d] = __float2bfloat16_rn(res[cnt]);
+        p.attn_out[(size_t)(hs + h) * D + d] = __float2bfloat16_rn(res[k]);
       } else {
         const size_t row = (size_t)(hs + h) * p.maxP + out_slot;
-        p.attn_o[row * D + d] = res[cnt];
+        p.attn_o[row * D + d] = res[k];
         if (d == 0) p.lse[row] = logf(den[h]);
       }
     }
     sync();
-    if (tid == 0) {
-      red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
-    }
+    if (tid == 0) red_release_add(bar(l, OP_REDUCTION - 1, 0), gqa);
   }
 
   // Epoch-tagged arrival counter: returns the arrival number (1-based) of this
@@ -654,6 +774,22 @@ struct Consumer {
     const int l = ins.w[1], b0 = ins.w[2], b1 = ins.w[3], split = ins.w[4];
     const int R = o ? p.o_R : p.down_R;
     const int splits = o ? p.o_splits : p.down_splits;
+    const int nrows = (b1 - b0) * 16;
+    // O-proj adds into the residual stream; with deferred down partials of
+    // layer l - 1 (complete before this layer's attention can finish, and in
+    // practice long before) the first row of each thread is read before the
+    // attention wait, so that its latency overlaps the wait
+    const bool own_rows = o && splits == 1 && p.tp_world <= 1;
+    const int nsplit = own_rows ? deferred_splits(l - 1) : 0;
+    float hpre = 0.f;
+    if (own_rows) {
+      if (nsplit > 0) {
+        int* a = bar(l - 1, OP_DOWN - 1, 0);
+        const int t = p.down_done_target;
+        if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
+      }
+      if (tid < nrows) hpre = residual_value(b0 * 16 + tid, nsplit);
+    }
     {
       int* a = o ? bar(l, OP_REDUCTION - 1, 0) : bar(l, OP_UPGATE - 1, 0);
       const int t = o ? p.Hq : p.I / 16;
@@ -668,7 +804,7 @@ struct Consumer {
     float* part = partials_after(R);
     gemv_stream(pl.ns, R, part);
     stamp(4);
-    if (o && p.tp_world > 1) {
+    if (kMixtral && o && p.tp_world > 1) {
       // tensor parallel: all-reduce the fp32 row partials over NVLink, then
       // add their rank-ordered sum, rounded once, to hidden (same on all ranks)
       for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
@@ -690,18 +826,22 @@ struct Consumer {
       if (tid == 0) red_release_add(bar(l, OP_OPROJ - 1, 0), b1 - b0);
       return;
     }
-    for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
+#pragma unroll 1
+    for (int idx = tid; idx < nrows; idx += NC) {
       const int j = idx / 16, r = idx % 16;
       const int row = (b0 + j) * 16 + r;
       const float v = bf16r(row_sum(part, j * spb, R, r));
-      if (splits == 1)
-        p.hidden[row] = __float2bfloat16_rn(ldcg_bf16(p.hidden + row) + v);
-      else
+      if (splits == 1) {
+        const float h = own_rows && idx == tid ? hpre : residual_value(row, nsplit);
+        p.hidden[row] = __float2bfloat16_rn(h + v);
+      } else {
         partials[(size_t)split * p.H + row] = __float2bfloat16_rn(v);
+      }
     }
     sync();
     int* done = bar(l, pl.op - 1, 0);
-    if (splits == 1) {
+    if (splits == 1 || (!o && l < p.defer_down)) {
+      // one writer per row, or split partials left for the next layer's readers
       if (tid == 0) red_release_add(done, b1 - b0);
       return;
     }
@@ -733,13 +873,14 @@ struct Consumer {
   // LayerNormDoubleMatVecSiLU (python_vm.py:142-179): silu(gate) * up per block.
   __device__ void op_upgate(const Ins& ins, const Plan& pl) {
     const int l = ins.w[1], n = ins.w[2];
+    const NormWeights nw = preload_norm(p.mlp_ln + (size_t)l * p.H, p.H);
     {
       int* a = bar(l, OP_OPROJ - 1, 0);
       const int t = p.H / 16;
       if (!wait_counters(1, &a, &t, OP_UPGATE, l)) { drain(pl.ns); return; }
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H);
+    rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H, nw);
     stamp(3);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
@@ -759,13 +900,14 @@ struct Consumer {
   // RMS_LM_Head (python_vm.py:265-288): logits rows of the final RMSNorm'd hidden.
   __device__ void op_lm_head(const Ins& ins, const Plan& pl) {
     const int b0 = ins.w[1], b1 = ins.w[2];
+    const NormWeights nw = preload_norm(p.lm_norm, p.H);
     {
       int* a = bar(p.L - 1, OP_DOWN - 1, 0);
       const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.lm_norm, p.H);
+    rmsnorm_to_act(p.hidden, p.lm_norm, p.H, nw);
     stamp(3);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
@@ -864,6 +1006,7 @@ struct Consumer {
   // RmsRouterUpgate (mixtral/python_vm.py:525-574).
   __device__ void op_router_upgate(const Ins& ins, const Plan& pl) {
     const int l = ins.w[1], b0 = ins.w[2], nb = ins.w[3];
+    const NormWeights nw = preload_norm(p.ffn_ln + (size_t)l * p.H, p.H);
     {
       int* a = bar(l, OP_OPROJ - 1, 0);
       const int t = p.H / 16;
@@ -875,7 +1018,7 @@ struct Consumer {
       }
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H);
+    rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H, nw);
     router(l);
     if (pl.ns > 0) handoff(rsel);
     if (tid < p.topk) {
@@ -976,13 +1119,14 @@ struct Consumer {
   // logits, and with two splits the sum is independent of their order).
   __device__ void op_lm_head_split(const Ins& ins, const Plan& pl) {
     const int b0 = ins.w[1], b1 = ins.w[2], split = ins.w[3];
+    const NormWeights nw = preload_norm(p.lm_norm, p.H);
     {
       int* a = bar(p.L - 1, OP_DOWN - 1, 0);
       const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.lm_norm, p.H);
+    rmsnorm_to_act(p.hidden, p.lm_norm, p.H, nw);
     stamp(3);
     const int spb = stages_per_row_block(LM_HEAD_SPLIT);
     float* part = partials_after(p.H);
@@ -1013,6 +1157,7 @@ struct Consumer {
   // SpeculativeExpertPredict (mixtral/python_vm.py:653-668).
   __device__ void op_predict(const Ins& ins) {
     const int l = ins.w[1];
+    const NormWeights nw = preload_norm(p.ffn_ln + (size_t)l * p.H, p.H);
     if (l > 0) {
       int* a = bar(l - 1, OP_DOWN - 1, 0);
       const int t = p.down_done_target;
@@ -1021,7 +1166,7 @@ struct Consumer {
       return;
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H);
+    rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H, nw);
     router(l);
     if (tid < p.topk) p.pred_idx[tid] = rsel[tid];
     sync();
@@ -1050,7 +1195,7 @@ struct PrefetchCursor {
         // Mixtral expert instructions: the predicted experts (a hint written
         // by SpeculativeExpertPredict; stale values only cost a wasted prefetch)
         int pred[MAX_TOPK] = {0, 0, 0, 0};
-        if (p.model == MODEL_MIXTRAL)
+        if (kMixtral)
           for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) pred[t] = ld_relaxed(p.pred_idx + t);
         wk.init(p, *ins, make_plan(p, *ins), pred);
         have = true;
@@ -1083,7 +1228,7 @@ __device__ void prefetch_instruction(const KParams& p, int q, int i, Ins* ins) {
   const Plan pl = make_plan(p, *ins);
   if (pl.bad_word >= 0 || pl.ns == 0 || pl.op == OP_PARTIAL) return;
   int pred[MAX_TOPK] = {0, 0, 0, 0};
-  if (p.model == MODEL_MIXTRAL)
+  if (kMixtral)
     for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) pred[t] = ld_relaxed(p.pred_idx + t);
   StageWalker w;
   w.init(p, *ins, pl, pred);
@@ -1104,6 +1249,77 @@ __device__ void prefetch_instruction(const KParams& p, int q, int i, Ins* ins) {
   }
 }
 
+// ------------------------------------------------------------------ MLP prefetcher
+// L2 prefetch of [src, src + bytes) by one warp in 16 KiB pieces: per-line
+// prefetches through the load/store unit (lane t takes lines t, t + 32, ...),
+// or TMA bulk prefetches (PF_BULK); an optional pause after each piece.
+__device__ __forceinline__ void warp_prefetch_l2(const KParams& p, const void* src, uint32_t bytes, int lane) {
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  constexpr uint32_t PIECE = 16384;
+  for (uint32_t o = 0; o < bytes; o += PIECE) {
+    const uint32_t n = min(PIECE, bytes - o);
+    if (p.pf_mlp & PF_BULK) {
+      if (lane == 0) bulk_prefetch_l2(s + o, n);
+    } else if (p.pf_mlp & PF_EVICT_LAST) {
+      for (uint32_t off = (uint32_t)lane * 128u; off < n; off += 32u * 128u) prefetch_l2_line_last(s + o + off);
+    } else {
+      for (uint32_t off = (uint32_t)lane * 128u; off < n; off += 32u * 128u) prefetch_l2_line(s + o + off);
+    }
+    if (p.pf_gap_ns > 0) __nanosleep(p.pf_gap_ns);
+  }
+}
+
+// The prefetcher warp walks its queue; for each Llama up/gate or down
+// instruction of layer l it waits until layer l - 1's down projection is
+// complete (from then on the SMs run the attention chain of layer l, whose
+// weights are already in the rings) and prefetches the instruction's weight
+// rows into L2. Its waits are bounded and it records no errors: on a timeout
+// or an aborted launch it simply stops (the consumers report the failure).
+__device__ void run_mlp_prefetcher(const KParams& p) {
+  const int q = blockIdx.x, lane = threadIdx.x & 31;
+  int armed = -1;  // layer whose trigger has been seen
+  for (int i = 0; i < p.Q; ++i) {
+    const int wv = __ldg(p.instructions + ((size_t)q * p.Q + i) * 32 + lane);  // lane t: word t
+    const int op = __shfl_sync(0xffffffffu, wv, 0), l = __shfl_sync(0xffffffffu, wv, 1);
+    const bool up = op == OP_UPGATE && (p.pf_mlp & PF_UPGATE);
+    const bool dn = op == OP_DOWN && (p.pf_mlp & PF_DOWN);
+    if ((!up && !dn) || l < 0 || l >= p.L) continue;
+    if (l != armed) {
+      if (l > 0) {
+        int ok = 1;
+        if (lane == 0) {
+          const int* c = p.barriers + ((size_t)(l - 1) * p.brow + (OP_DOWN - 1)) * p.bcol;
+          const uint64_t t0 = globaltimer();
+          while (ld_relaxed(c) < p.down_done_target) {
+            if (aborted(p) || (long long)(globaltimer() - t0) > p.timeout_ns) { ok = 0; break; }
+            __nanosleep(64);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+      }
+      armed = l;
+    }
+    if (up) {
+      const int n = __shfl_sync(0xffffffffu, wv, 2);
+      if (n < 0 || n > 29) continue;
+      for (int j = 0; j < n; ++j) {
+        const int b = __shfl_sync(0xffffffffu, wv, 3 + j);
+        if (b < 0 || b >= p.I / 16) continue;
+        const size_t row = (size_t)l * p.I + (size_t)b * 16;
+        warp_prefetch_l2(p, p.w_up + row * p.H, 16u * p.H * 2u, lane);
+        warp_prefetch_l2(p, p.w_gate + row * p.H, 16u * p.H * 2u, lane);
+      }
+    } else {
+      const int b0 = __shfl_sync(0xffffffffu, wv, 2), b1 = __shfl_sync(0xffffffffu, wv, 3);
+      const int split = __shfl_sync(0xffffffffu, wv, 4);
+      if (b0 < 0 || b1 > p.H / 16 || b0 > b1 || split < 0 || split >= p.down_splits) continue;
+      for (int r = b0 * 16; r < b1 * 16; ++r)
+        warp_prefetch_l2(p, p.w_down + ((size_t)l * p.H + r) * p.I + (size_t)split * p.down_R,
+                         (uint32_t)p.down_R * 2u, lane);
+    }
+  }
+}
+
 // lins / pins: shared-memory instruction buffers of the loader and of its L2
 // prefetch cursor (dynamically indexed words stay out of local memory).
 __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_t* mbox_bar, Ins* lins,
@@ -1117,16 +1333,18 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
   long long g_load = 0;
   uint32_t mbox_phase = 0;
   const long long ring_timeout = 4 * p.timeout_ns + 2000000000ll;
+  const bool ring_ef = (p.pf_mlp & PF_RING_EVICT_FIRST) != 0;
+  const uint64_t pol_ef = policy_evict_first();
 
   for (int i = 0; i < p.Q; ++i) {
     fetch_ins(p, q, i, ins);
     const Plan pl = make_plan(p, ins);
     int ex[MAX_TOPK] = {0, 0, 0, 0};
-    if (p.model == MODEL_MIXTRAL && (pl.op == OP_UPGATE || pl.op == OP_DOWN) && pl.bad_word < 0 && pl.ns > 0) {
+    if (kMixtral && (pl.op == OP_UPGATE || pl.op == OP_DOWN) && pl.bad_word < 0 && pl.ns > 0) {
       // which experts to stream is decided by the consumers (router, or the
       // router outputs of another SM): wait for their handoff, prefetching
       // ahead into L2 meanwhile
-      while (p.pf_stages > 0 && pf.g < g_load + p.pf_stages && !mbar_test_wait(mbox_bar, mbox_phase))
+      while (kPrefetch && p.pf_stages > 0 && pf.g < g_load + p.pf_stages && !mbar_test_wait(mbox_bar, mbox_phase))
         if (!pf.step(p, q, g_load)) break;
       if (!ring_wait(mbox_bar, mbox_phase, ring_timeout)) {
         record_error(p, 4, i, pl.op, pl.layer, -1, (int)mbox_phase, -2);
@@ -1136,9 +1354,9 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
       for (int t = 0; t < p.topk && t < MAX_TOPK; ++t) ex[t] = mbox[t];
     }
     wk.init(p, ins, pl, ex);
-    if (p.pf_next == 1) {
+    if (kPrefetch && p.pf_next == 1) {
       prefetch_instruction(p, q, i + 1, pins);
-    } else if (p.pf_next == 2 && pl.op >= OP_QKV && pl.op <= OP_OPROJ && pl.layer != pf_layer) {
+    } else if (kPrefetch && p.pf_next == 2 && pl.op >= OP_QKV && pl.op <= OP_OPROJ && pl.layer != pf_layer) {
       pf_layer = pl.layer;
       for (int j = i + 1; j < p.Q; ++j) {
         const int* wj = p.instructions + ((size_t)q * p.Q + j) * 32;
@@ -1155,7 +1373,7 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
           uint64_t* empty = &ring.empty[ring.slot];
           const uint32_t parity = ring.phase ^ 1u;
           if (!mbar_test_wait(empty, parity)) {
-            bool more = p.pf_stages > 0;
+            bool more = kPrefetch && p.pf_stages > 0;
             while (more && pf.g < g_load + p.pf_stages && !mbar_test_wait(empty, parity))
               more = pf.step(p, q, g_load);
             if (!ring_wait(empty, parity, ring_timeout)) {
@@ -1168,7 +1386,10 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
           uint64_t* fb = &ring.full[ring.slot];
           uint8_t* dst = ring.stages + (size_t)ring.slot * STAGE_BYTES;
           mbar_arrive_expect_tx(fb, rr.bytes * (uint32_t)rr.copies);
-          for (int c = 0; c < rr.copies; ++c) bulk_load(dst + c * rr.bytes, rr.src + c * rr.row_step, rr.bytes, fb);
+          if (ring_ef)
+            for (int c = 0; c < rr.copies; ++c) bulk_load_hint(dst + c * rr.bytes, rr.src + c * rr.row_step, rr.bytes, fb, pol_ef);
+          else
+            for (int c = 0; c < rr.copies; ++c) bulk_load(dst + c * rr.bytes, rr.src + c * rr.row_step, rr.bytes, fb);
           rr.src += rr.stage_step;
           ring_advance(ring);
           ++g_load;
@@ -1180,7 +1401,7 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
       const uint32_t parity = ring.phase ^ 1u;
       if (!mbar_test_wait(empty, parity)) {
         // ring full: run the L2 prefetch ahead while waiting for a slot
-        bool more = p.pf_stages > 0;
+        bool more = kPrefetch && p.pf_stages > 0;
         while (more && pf.g < g_load + p.pf_stages && !mbar_test_wait(empty, parity))
           more = pf.step(p, q, g_load);
         if (!ring_wait(empty, parity, ring_timeout)) {
@@ -1202,7 +1423,11 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
   }
 }
 
+}  // namespace
+
 // ------------------------------------------------------------------ kernel
+namespace EK_NS {
+
 template <int D>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ KParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -1237,8 +1462,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   __syncthreads();
 
   Ring ring{stages, full, empty, 0, 0u, 0u};
-  if (warp == CW) {
+  if (warp == LOADER_WARP) {
     if (lane == 0) run_loader(p, ring, mbox, mbox_bar, ins_smem + 1, ins_smem + 2);
+    return;
+  }
+  if (kPrefetch && warp == PREFETCH_WARP) {
+    if ((p.pf_mlp & (PF_UPGATE | PF_DOWN)) && !kMixtral) run_mlp_prefetcher(p);
     return;
   }
 
@@ -1268,12 +1497,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     c.stamp(0);
     if (pl.bad_word >= 0) {
       if (tid == 0)
-        record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > (p.model == MODEL_MIXTRAL ? OP_PREDICT : OP_LM_HEAD)) ? 2 : 3, i, pl.op,
+        record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > (kMixtral ? OP_PREDICT : OP_LM_HEAD)) ? 2 : 3, i, pl.op,
                      pl.layer, 0, pl.bad_word, ins.w[pl.bad_word]);
       c.sync();  // before the next instruction's words overwrite these
       continue;  // no stages were planned for it
     }
-    if (p.model == MODEL_MIXTRAL && pl.op >= OP_UPGATE) {
+    if (kMixtral && pl.op >= OP_UPGATE) {
       switch (pl.op) {
         case OP_UPGATE: c.op_router_upgate(ins, pl); break;
         case OP_DOWN: c.op_expert_down(ins, pl); break;
@@ -1301,7 +1530,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   }
   // tensor parallel: the logits are complete once every rank's LM-head
   // instructions have added into them; block 0 holds the kernel until then
-  if (p.model == MODEL_MIXTRAL && p.tp_world > 1 && p.tp_lm_count > 0 && blockIdx.x == 0) {
+  if (kMixtral && p.tp_world > 1 && p.tp_lm_count > 0 && blockIdx.x == 0) {
     int* a = c.tp_counter(p.tp_rank, p.tp_off_cnt_lm, 0);
     const int t = p.tp_world * p.tp_lm_count * (int)p.tp_step;
     c.iidx = p.Q;
@@ -1310,15 +1539,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
 }
 
 // ------------------------------------------------------------------ host launch
-cudaError_t launch_decode(const KParams& p, cudaStream_t stream) {
-  static bool attr_done[2] = {false, false};
+cudaError_t launch(const KParams& p, cudaStream_t stream) {
+  // The shared-memory opt-in is a per-device function attribute: set it once
+  // per (device, head_dim) variant. Devices beyond the table set it on every
+  // launch (cheap, and idempotent).
+  constexpr int kDevs = 64;
+  static std::atomic<unsigned char> attr_done[kDevs][2];
   const void* fn = p.D == 64 ? reinterpret_cast<const void*>(&decode_kernel<64>)
                              : reinterpret_cast<const void*>(&decode_kernel<128>);
   const int which = p.D == 64 ? 0 : 1;
-  if (!attr_done[which]) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kDevs || !attr_done[dev][which].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr_done[which] = true;
+    if (dev >= 0 && dev < kDevs) attr_done[dev][which].store(1, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nq);
@@ -1333,5 +1569,7 @@ cudaError_t launch_decode(const KParams& p, cudaStream_t stream) {
   if (p.D == 64) return cudaLaunchKernelEx(&cfg, decode_kernel<64>, p);
   return cudaLaunchKernelEx(&cfg, decode_kernel<128>, p);
 }
+
+}  // namespace EK_NS
 
 }  // namespace ek

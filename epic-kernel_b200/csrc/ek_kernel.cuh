@@ -33,11 +33,29 @@
 
 #include "ek_ptx.cuh"
 
+// Compile-time variant of the translation unit that includes this header
+// (ek_decode.cu is compiled once per variant, so that each kernel carries only
+// the code its model runs: a megakernel's code must stay small enough for the
+// SM's instruction cache).
+//   EK_MODEL 0: Llama opcodes 1-7; 1: Mixtral opcodes 1-8 (and tensor parallel)
+//   EK_PF    0: no L2 prefetch paths; 1: the optional L2 prefetch modes
+#ifndef EK_MODEL
+#define EK_MODEL 0
+#endif
+#ifndef EK_PF
+#define EK_PF 0
+#endif
+
 namespace ek {
+
+constexpr bool kMixtral = EK_MODEL == 1;
+constexpr bool kPrefetch = EK_PF == 1;
 
 constexpr int CW = 8;                 // consumer warps
 constexpr int NC = CW * 32;           // consumer threads
-constexpr int NTHREADS = NC + 32;     // + loader warp
+constexpr int LOADER_WARP = CW;       // warp index of the ring loader
+constexpr int PREFETCH_WARP = CW + 1; // warp index of the MLP-weight L2 prefetcher (prefetch variant)
+constexpr int NTHREADS = NC + (kPrefetch ? 64 : 32);  // + loader warp (+ prefetcher warp)
 constexpr int STAGE_BYTES = 16384;    // one ring stage
 constexpr int HALF_STAGE = 8192;      // one TMA box (16 rows x 256 bf16, or TK x D bf16)
 constexpr int ACT_BYTES = 49152;      // activation vector + per-stage partial sums / attention merge
@@ -53,7 +71,7 @@ constexpr int MAX_GQA = 4;  // query heads per KV head
 constexpr int MAX_EXPERTS = 16;
 constexpr int MAX_TOPK = 4;
 constexpr int LM_HEAD_SPLIT = 2048;
-constexpr int MAX_TP = 8;  // Mixtral LM-head column split (python_vm.py:630)
+constexpr int MAX_TP = 8;  // most tensor-parallel ranks (symmetric buffers mapped per launch)
 
 enum Op : int {
   OP_NOOP = 0,
@@ -65,6 +83,15 @@ enum Op : int {
   OP_DOWN = 6,
   OP_LM_HEAD = 7,
   OP_PREDICT = 8,  // Mixtral SpeculativeExpertPredict
+};
+
+enum CacheBits : int {
+  PF_UPGATE = 1,
+  PF_DOWN = 2,
+  PF_BULK = 4,
+  PF_EVICT_LAST = 8,
+  PF_RING_EVICT_FIRST = 16,
+  PF_KV_EVICT_FIRST = 32,
 };
 
 enum Model : int { MODEL_LLAMA = 0, MODEL_MIXTRAL = 1 };
@@ -142,6 +169,22 @@ struct KParams {
   // loading; 2 = this queue's up/gate and down weights of a layer when its
   // first attention-chain instruction (opcodes 1-4) starts loading.
   int pf_next;
+  // EK_CACHE_* bits (include/ek.h). Prefetch bits (prefetch variant only):
+  // L2 prefetch of a layer's MLP weights by the prefetcher warp, issued once
+  // the previous layer's down projection is complete.
+  int pf_mlp;
+  unsigned pf_gap_ns;  // pause of the prefetcher warp after each 16 KiB it requests
+  // Llama with column-split down projections (and one O-proj split): layers
+  // l < defer_down publish only their bf16 split partials; the next readers
+  // of the residual stream (layer l + 1's QKV RMSNorm and O-proj residual add)
+  // add them to `hidden` in split order, the interpreter's order and rounding.
+  // The last layer of the instruction stream adds them itself, so the LM head
+  // and the caller see the final hidden state.
+  int defer_down;
+  // The last PartialAttention of a KV head to finish runs that head's
+  // AttentionReduction; the reduction instructions become no-ops. Only for
+  // schedules whose reductions are terminal over all partials in order.
+  int fuse_red;
   long long timeout_ns;
   unsigned epoch;
 };
@@ -230,7 +273,7 @@ struct Plan {
   int bad_word;   // >= 0: index of an out-of-range word
 };
 
-__device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
+static __device__ __noinline__ Plan make_plan(const KParams& p, const Ins& ins) {
   Plan pl;
   pl.op = ins.w[0];
   pl.layer = 0;
@@ -241,7 +284,7 @@ __device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
     pl.bad_word = idx;
     pl.ns = 0;
   };
-  if (p.model == MODEL_MIXTRAL && pl.op >= OP_UPGATE && pl.op <= OP_PREDICT) {
+  if (kMixtral && pl.op >= OP_UPGATE && pl.op <= OP_PREDICT) {
     switch (pl.op) {
       case OP_UPGATE: {  // RmsRouterUpgate: layer, start_block, num_blocks
         pl.layer = w[1];
@@ -359,7 +402,7 @@ __device__ __forceinline__ bool aborted(const KParams& p) {
   return ld_relaxed(reinterpret_cast<const int*>(&p.status->abort_epoch)) == (int)p.epoch;
 }
 
-__device__ inline void record_error(const KParams& p, int code, int instr, int opcode, int layer,
+static __device__ __noinline__ void record_error(const KParams& p, int code, int instr, int opcode, int layer,
                              int observed, int expected, int detail) {
   if (atomicCAS(&p.status->code, 0, -1) == 0) {
     p.status->sm = blockIdx.x;
@@ -395,7 +438,7 @@ struct StageWalker {
   int kv_t0, kv_head;
 
   __device__ __forceinline__ long long block_row(const KParams& p, int jj) const {
-    if (p.model == MODEL_MIXTRAL) {
+    if (kMixtral) {
       const long long e = (long long)w[1] * p.E + experts[es];
       switch (op) {
         case OP_UPGATE: return e * p.I + (long long)(w[2] + jj) * 16;
@@ -415,7 +458,7 @@ struct StageWalker {
 
   // `ex`: the selected (or, for prefetch, predicted) experts of a Mixtral
   // expert instruction; ignored otherwise.
-  __device__ __forceinline__ void init(const KParams& p, const Ins& ins, const Plan& pl, const int* ex = nullptr) {
+  __device__ __noinline__ void init(const KParams& p, const Ins& ins, const Plan& pl, const int* ex = nullptr) {
     op = pl.op;
     k = 0;
     ns = pl.ns;
@@ -425,7 +468,7 @@ struct StageWalker {
     es = 0;
     ne = 1;
     nblocks = 1 << 30;
-    if (p.model == MODEL_MIXTRAL && (op == OP_UPGATE || op == OP_DOWN || op == OP_LM_HEAD)) {
+    if (kMixtral && (op == OP_UPGATE || op == OP_DOWN || op == OP_LM_HEAD)) {
       if (op == OP_UPGATE) {
         mat[0] = p.w_egate; mat[1] = p.w_eup; nmat = 2; mat_rows = p.rows_eup;
         stride = p.H; S = p.H; nblocks = w[3]; ne = p.topk;
@@ -474,7 +517,7 @@ struct StageWalker {
   // Issue the current stage (load into dst completing on bar, or an L2
   // prefetch) and advance. Returns the stage's bytes.
   template <bool PREFETCH>
-  __device__ __forceinline__ uint32_t issue(const KParams& p, uint8_t* dst, uint64_t* bar) {
+  __device__ __noinline__ uint32_t issue(const KParams& p, uint8_t* dst, uint64_t* bar) {
     uint32_t bytes;
     if (op == OP_PARTIAL) {
       const int t0 = kv_t0 + k * p.tk;
@@ -483,8 +526,14 @@ struct StageWalker {
         tma_prefetch_3d(&p.tm_v, 0, kv_head, t0);
       } else {
         mbar_arrive_expect_tx(bar, 2 * HALF_STAGE);
-        tma_load_3d(dst, &p.tm_k, 0, kv_head, t0, bar);
-        tma_load_3d(dst + HALF_STAGE, &p.tm_v, 0, kv_head, t0, bar);
+        if (p.pf_mlp & PF_KV_EVICT_FIRST) {
+          const uint64_t pol = policy_evict_first();
+          tma_load_3d_hint(dst, &p.tm_k, 0, kv_head, t0, bar, pol);
+          tma_load_3d_hint(dst + HALF_STAGE, &p.tm_v, 0, kv_head, t0, bar, pol);
+        } else {
+          tma_load_3d(dst, &p.tm_k, 0, kv_head, t0, bar);
+          tma_load_3d(dst + HALF_STAGE, &p.tm_v, 0, kv_head, t0, bar);
+        }
       }
       bytes = 2 * HALF_STAGE;
     } else {
@@ -508,8 +557,14 @@ struct StageWalker {
         else for (int i = 0; i < rps; ++i) bulk_prefetch_l2(src + (size_t)i * stride, row_bytes);
       } else {
         mbar_arrive_expect_tx(bar, bytes);
-        if (whole) bulk_load(dst, src, bytes, bar);
-        else for (int i = 0; i < rps; ++i) bulk_load(dst + i * row_bytes, src + (size_t)i * stride, row_bytes, bar);
+        if (p.pf_mlp & PF_RING_EVICT_FIRST) {
+          const uint64_t pol = policy_evict_first();
+          if (whole) bulk_load_hint(dst, src, bytes, bar, pol);
+          else for (int i = 0; i < rps; ++i) bulk_load_hint(dst + i * row_bytes, src + (size_t)i * stride, row_bytes, bar, pol);
+        } else {
+          if (whole) bulk_load(dst, src, bytes, bar);
+          else for (int i = 0; i < rps; ++i) bulk_load(dst + i * row_bytes, src + (size_t)i * stride, row_bytes, bar);
+        }
       }
     }
     advance(p);
@@ -528,7 +583,7 @@ struct StageWalker {
     int copies;
     long long row_step, stage_step;
   };
-  __device__ __forceinline__ int contiguous_run(const KParams& p, Run& r) {
+  __device__ __noinline__ int contiguous_run(const KParams& p, Run& r) {
     if (op == OP_PARTIAL || chunks != 1) return 0;
     int n = groups - rg;
     if (nmat == 1) n = (int)min((long long)(ns - k), (long long)(nblocks - j) * groups - rg);
@@ -547,7 +602,7 @@ struct StageWalker {
   }
 
   // Advance over a run of n stages returned by contiguous_run.
-  __device__ __forceinline__ void skip_run(const KParams& p, int n) {
+  __device__ __noinline__ void skip_run(const KParams& p, int n) {
     k += n;
     if (nmat == 1) {
       rg += n;

@@ -47,6 +47,15 @@ def interpret_with_mk(globs: Globals, mk_func, **options):
     )
 
 
+def _stream_options(globs, options):
+    """Engine options that depend on the instruction stream, as
+    `tensorize_instructions` recorded them on `globs` (explicit options win)."""
+    opts = dict(options)
+    opts.setdefault("fuse_attention_reduction", getattr(globs, "attention_reduction_fusable", False))
+    opts.setdefault("deferred_down_layers", getattr(globs, "deferrable_down_layers", 0))
+    return opts
+
+
 class LatencyMK_Interpreter(MK_Interpreter):
     """`options` are passed to every launch (e.g. l2_prefetch_stages)."""
 
@@ -55,7 +64,7 @@ class LatencyMK_Interpreter(MK_Interpreter):
         self.options = options
 
     def interpret(self, globs: Globals):
-        interpret_with_mk(globs, self.mk_func, **self.options)
+        interpret_with_mk(globs, self.mk_func, **_stream_options(globs, self.options))
 
 
 class Latency3B_MK_Interpreter(MK_Interpreter):
@@ -67,4 +76,4 @@ class Latency3B_MK_Interpreter(MK_Interpreter):
         self.options = options
 
     def interpret(self, globs: Globals):
-        interpret_with_mk(globs, self.mk_func, **self.options)
+        interpret_with_mk(globs, self.mk_func, **_stream_options(globs, self.options))

@@ -15,7 +15,7 @@ import torch
 PKG_ROOT = Path(__file__).resolve().parent.parent  # the directory holding mk_llama.py
 LIB_PATH = PKG_ROOT / "libek.so"
 
-EK_ABI_VERSION = 1
+EK_ABI_VERSION = 2
 
 STATUS_NAMES = {
     0: "ok",
@@ -66,6 +66,8 @@ class EkLlamaArgs(ctypes.Structure):
         ("down_reduction_size", _I), ("oproj_reduction_size", _I),
         ("l2_prefetch_stages", _I), ("record_timings", _I),
         ("timeout_ns", ctypes.c_int64),
+        ("cache_flags", _I), ("prefetch_gap_ns", _I),
+        ("options", _I), ("deferred_down_layers", _I),
     ]
 
 
@@ -90,6 +92,7 @@ class EkMixtralArgs(ctypes.Structure):
         ("skip_attn_reduction", _I),
         ("l2_prefetch_stages", _I), ("record_timings", _I),
         ("timeout_ns", ctypes.c_int64),
+        ("cache_flags", _I), ("prefetch_gap_ns", _I),
         ("tp_lm_instructions", _I),
     ]
 

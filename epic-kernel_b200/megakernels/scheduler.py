@@ -232,6 +232,8 @@ def tensorize_instructions(globs: BaseGlobals, instruction_queues: list[list[Ins
     for q in instruction_queues:
         q.extend([NoOp()] * (queue_len - len(q)))
 
+    globs.attention_reduction_fusable = attention_reduction_fusable(globs, instruction_queues)
+    globs.deferrable_down_layers = deferrable_down_layers(instruction_queues)
     words = [serialize_and_pad(ins) for q in instruction_queues for ins in q]
     globs.instructions = torch.tensor(words, dtype=torch.int32).view(
         num_sms, queue_len, INTS_PER_INSTRUCTION
@@ -239,3 +241,57 @@ def tensorize_instructions(globs: BaseGlobals, instruction_queues: list[list[Ins
     globs.timings = torch.zeros(
         [num_sms, queue_len, TIMING_SLOTS], dtype=torch.int32, device=globs.device
     )
+
+
+def attention_reduction_fusable(globs, instruction_queues) -> bool:
+    """True when the attention merges of these queues can be done by the last
+    PartialAttention (opcode 2) of each KV head instead of by the
+    AttentionReduction (opcode 3) instructions: every reduction is terminal
+    over all partials of its head group, in order, one per (layer, group), and
+    each group's partials are exactly partial_idx 0..P-1 of one P. The engine
+    then produces the same outputs and counter values (an engine option; the
+    instruction stream itself is unchanged)."""
+    heads = getattr(globs, "num_attention_heads", None)
+    kv = getattr(globs, "num_kv_heads", None)
+    if not heads or not kv:
+        return False
+    gqa = heads // kv
+    reductions, partials = {}, {}
+    for q in instruction_queues:
+        for ins in q:
+            op = ins.opcode()
+            if op == 3:
+                key = (ins.layer_idx, ins.head_start_idx)
+                if (key in reductions or not ins.is_terminal or ins.head_start_idx % gqa
+                        or list(ins.reduction_list) != list(range(ins.num_partials))):
+                    return False
+                reductions[key] = ins.num_partials
+            elif op == 2:
+                partials.setdefault((ins.layer_idx, ins.kv_head_idx), []).append(
+                    (ins.num_partials, ins.partial_idx))
+    if not reductions:
+        return False
+    for (layer, kv_head), parts in partials.items():
+        n = parts[0][0]
+        if sorted(parts) != [(n, i) for i in range(n)]:
+            return False
+        if n > 1 and reductions.get((layer, kv_head * gqa)) != n:
+            return False
+    return len(reductions) == sum(1 for parts in partials.values() if parts[0][0] > 1)
+
+
+def deferrable_down_layers(instruction_queues) -> int:
+    """Number of leading layers l whose DownProjResidual (opcode 6) may leave
+    its column-split partials for layer l + 1 to add: the stream holds layer
+    l's down projection and layer l + 1's QKV (opcode 1) and O_ProjResidual
+    (opcode 4), the two readers of the residual stream that add them."""
+    ops = {}
+    for q in instruction_queues:
+        for ins in q:
+            op = ins.opcode()
+            if op in (1, 4, 6):
+                ops.setdefault(op, set()).add(ins.layer_idx)
+    n = 0
+    while n in ops.get(6, ()) and n + 1 in ops.get(1, ()) and n + 1 in ops.get(4, ()):
+        n += 1
+    return n

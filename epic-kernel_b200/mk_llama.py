@@ -21,6 +21,20 @@ Extra keyword-only options (defaults match the reference's behaviour):
                       timings[q, i, 0..2]
   down_reduction_size columns per DownProjResidual split (default gcd(I, H),
                       as the schedule builder uses)
+  cache_flags         EK_CACHE_* bits of include/ek.h (default: weight loads
+                      marked evict_first)
+  prefetch_gap_ns     pause of the optional MLP-weight prefetcher per 16 KiB
+  fuse_attention_reduction
+                      the last PartialAttention of each KV head merges the
+                      head's partials and AttentionReduction instructions do
+                      nothing (only for schedules whose reductions are
+                      terminal over all partials in order; the interpreter
+                      sets it when `tensorize_instructions` found that)
+  deferred_down_layers
+                      down projections of layers l < this value leave their
+                      column-split partials for layer l + 1 to add (the
+                      interpreter passes what `tensorize_instructions` found
+                      safe for the stream)
 
 Errors: bad shapes or dtypes raise ValueError before launch; a CUDA launch
 failure raises RuntimeError. Device-side failures (timeouts, malformed
@@ -38,6 +52,18 @@ from megakernels import ek
 _BF16 = torch.bfloat16
 _cache: dict = {}
 
+# EK_CACHE_* bits (include/ek.h). Weight loads are marked evict_first by
+# default, so the small cross-SM working set (counters, activations,
+# instructions) stays in L2 while 2.5+ GB of weights stream through it.
+EK_CACHE_PREFETCH_UPGATE = 1
+EK_CACHE_PREFETCH_DOWN = 2
+EK_CACHE_PREFETCH_BULK = 4
+EK_CACHE_PREFETCH_EVICT_LAST = 8
+EK_CACHE_WEIGHTS_EVICT_FIRST = 16
+EK_CACHE_KV_EVICT_FIRST = 32
+DEFAULT_CACHE_FLAGS = EK_CACHE_WEIGHTS_EVICT_FIRST
+EK_OPT_FUSE_ATTENTION_REDUCTION = 1
+
 
 def _need(t: torch.Tensor, name: str, dtype, ndim: int | None = None):
     if not isinstance(t, torch.Tensor):
@@ -53,7 +79,9 @@ def _need(t: torch.Tensor, name: str, dtype, ndim: int | None = None):
     return t.data_ptr()
 
 
-def _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size):
+def _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size,
+                cache_flags=None, prefetch_gap_ns=0, fuse_attention_reduction=False,
+                deferred_down_layers=0):
     (barriers, instructions, timings, qkv_w, attn_ln_w, o_w, mlp_ln_w, up_w, gate_w, down_w,
      lm_norm_w, lm_w, k4, v4, cos, sin, hidden, q, attn_out, lse, o_int, silu, logits) = tensors
     a = ek.EkLlamaArgs()
@@ -121,6 +149,10 @@ def _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_re
     a.l2_prefetch_stages = l2_prefetch_stages
     a.record_timings = int(bool(record_timings))
     a.timeout_ns = int(timeout_ns)
+    a.cache_flags = int(DEFAULT_CACHE_FLAGS if cache_flags is None else cache_flags)
+    a.prefetch_gap_ns = int(prefetch_gap_ns)
+    a.options = EK_OPT_FUSE_ATTENTION_REDUCTION if fuse_attention_reduction else 0
+    a.deferred_down_layers = int(deferred_down_layers)
     return a, next(iter(devices)).index
 
 
@@ -135,17 +167,24 @@ def mk_llama(
     pos_id, attn_scale, rms_norm_eps, skip_attn_reduction,
     *, stream=None, l2_prefetch_stages: int = 0, record_timings: bool = False,
     timeout_ns: int = 0, down_reduction_size: int = 0,
+    cache_flags: int | None = None, prefetch_gap_ns: int = 0, fuse_attention_reduction: bool = False,
+    deferred_down_layers: int = 0,
 ):
     tensors = (barriers, instructions, timings, qkv_proj_weights, attn_ln_weights, o_proj_weights,
                mlp_ln_weights, up_proj_weights, gate_proj_weights, down_proj_weights,
                lm_head_norm_weights, lm_head_weights, k_cache, v_cache, rope_cos, rope_sin,
                hidden_states, post_ln_rope_q, attn_out, attn_lse_intermediates,
                attn_out_intermediates, silu_out, logits)
+    if cache_flags is None:
+        cache_flags = DEFAULT_CACHE_FLAGS
     key = (tuple((t.data_ptr(), tuple(t.shape), t.dtype) if t is not None else None for t in tensors),
-           l2_prefetch_stages, bool(record_timings), int(timeout_ns), down_reduction_size)
+           l2_prefetch_stages, bool(record_timings), int(timeout_ns), down_reduction_size,
+           int(cache_flags), int(prefetch_gap_ns), bool(fuse_attention_reduction), int(deferred_down_layers))
     hit = _cache.get(key)
     if hit is None:
-        hit = _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size)
+        hit = _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size,
+                          cache_flags, prefetch_gap_ns, bool(fuse_attention_reduction),
+                          int(deferred_down_layers))
         if len(_cache) > 64:
             _cache.clear()
         _cache[key] = hit

@@ -17,13 +17,14 @@ import ctypes
 import torch
 
 from megakernels import ek
-from mk_llama import _need, check, read_status
+from mk_llama import DEFAULT_CACHE_FLAGS, _need, check, read_status
 
 _BF16 = torch.bfloat16
 _cache: dict = {}
 
 
-def _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions=0):
+def _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions=0,
+           cache_flags=DEFAULT_CACHE_FLAGS, prefetch_gap_ns=0):
     (barriers, instructions, timings, qkv_w, attn_ln_w, o_w, eg, eu, ed, router_w, ffn_ln_w, lm_norm, lm_w,
      k4, v4, cos, sin, hidden, q, attn_out, lse, o_int, esilu, rnormed, logits, sel, scores, pred) = t
     a = ek.EkMixtralArgs()
@@ -89,6 +90,8 @@ def _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions
     a.record_timings = int(bool(record_timings))
     a.timeout_ns = int(timeout_ns)
     a.tp_lm_instructions = int(tp_lm_instructions)
+    a.cache_flags = int(cache_flags)
+    a.prefetch_gap_ns = int(prefetch_gap_ns)
     return a, hidden.device.index
 
 
@@ -103,18 +106,22 @@ def mk_mixtral(
     selected_expert_indices, selected_expert_scores, predicted_expert_indices,
     pos_id, attn_scale, rms_norm_eps, skip_attn_reduction,
     *, stream=None, l2_prefetch_stages: int = 0, record_timings: bool = False, timeout_ns: int = 0,
-    tp_lm_instructions: int = 0,
+    tp_lm_instructions: int = 0, cache_flags: int | None = None, prefetch_gap_ns: int = 0,
 ):
     t = (barriers, instructions, timings, qkv_weights, attn_norm_weights, o_weights, expert_gate_weights,
          expert_up_weights, expert_down_weights, router_weights, ffn_ln_weights, lm_head_norm_weights,
          lm_head_weights, k_cache, v_cache, rope_cos, rope_sin, hidden_states, q_post_rope, attn_out,
          attn_lse_intermediates, attn_out_intermediates, expert_silu_out, router_normed_hidden, logits,
          selected_expert_indices, selected_expert_scores, predicted_expert_indices)
+    if cache_flags is None:
+        cache_flags = DEFAULT_CACHE_FLAGS
     key = (tuple((x.data_ptr(), tuple(x.shape), x.dtype) if x is not None else None for x in t),
-           l2_prefetch_stages, bool(record_timings), int(timeout_ns), int(tp_lm_instructions))
+           l2_prefetch_stages, bool(record_timings), int(timeout_ns), int(tp_lm_instructions),
+           int(cache_flags), int(prefetch_gap_ns))
     hit = _cache.get(key)
     if hit is None:
-        hit = _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions)
+        hit = _build(t, l2_prefetch_stages, record_timings, timeout_ns, tp_lm_instructions,
+                     cache_flags, prefetch_gap_ns)
         if len(_cache) > 64:
             _cache.clear()
         _cache[key] = hit

@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define EK_ABI_VERSION 1
+#define EK_ABI_VERSION 2
 
 /* host return codes */
 #define EK_SUCCESS 0
@@ -39,6 +39,21 @@ extern "C" {
 #define EK_STATUS_RING_TIMEOUT 4    /* internal load ring stalled (engine bug) */
 #define EK_STATUS_BAD_COPY 5        /* a weight copy failed its bounds check (engine bug) */
 
+/* cache_flags bits (EkLlamaArgs / EkMixtralArgs) */
+#define EK_CACHE_PREFETCH_UPGATE 1   /* L2-prefetch a layer's up/gate rows once the previous layer is done */
+#define EK_CACHE_PREFETCH_DOWN 2     /* same for the down-projection rows */
+#define EK_CACHE_PREFETCH_BULK 4     /* prefetch with TMA bulk prefetches instead of per-line prefetches */
+#define EK_CACHE_PREFETCH_EVICT_LAST 8 /* prefetched lines get evict_last priority */
+#define EK_CACHE_WEIGHTS_EVICT_FIRST 16 /* weight loads marked evict_first (read once per step) */
+#define EK_CACHE_KV_EVICT_FIRST 32   /* KV-cache loads marked evict_first */
+
+/* EkLlamaArgs.options bits */
+/* The last PartialAttention of each KV head to finish merges the head's
+ * partials, and the AttentionReduction instructions do nothing. Valid only for
+ * schedules whose reductions are terminal over all partials in order (the
+ * latency scheduler's); the counters end with the same values. */
+#define EK_OPT_FUSE_ATTENTION_REDUCTION 1
+
 typedef struct EkContext EkContext;
 
 /* First device-side failure since the status was last cleared. */
@@ -50,7 +65,8 @@ typedef struct EkStatus {
   int32_t layer;
   int32_t observed; /* counter value last seen (timeouts) */
   int32_t expected; /* counter value waited for (timeouts) / bad word index */
-  int32_t detail;   /* barrier slot (timeouts) / offending word value */
+  int32_t detail;   /* timeouts: index of the counter in `barriers` (-1: a tensor-parallel counter
+                       in the symmetric buffer); bad instructions: offending word value */
 } EkStatus;
 
 /*
@@ -103,6 +119,14 @@ typedef struct EkLlamaArgs {
                                    weights prefetched into L2; 0 = off */
   int32_t record_timings;       /* write timings[q, i, 0..2] when timings != NULL */
   int64_t timeout_ns;           /* bound of every cross-SM wait; <= 0 selects 1 s */
+  int32_t cache_flags;          /* EK_CACHE_* bits: L2 eviction hints and MLP-weight L2 prefetch */
+  int32_t prefetch_gap_ns;      /* pause of the MLP prefetcher after each 16 KiB it requests (0 = none) */
+  int32_t options;              /* EK_OPT_* bits */
+  /* Down projections of layers l < deferred_down_layers leave their column-split
+   * partial sums for layer l + 1's QKV and O-proj to add into the residual
+   * stream (same order and rounding as adding them at once). The instruction
+   * stream must then hold layer l + 1's QKV and O-proj instructions; 0 = off. */
+  int32_t deferred_down_layers;
 } EkLlamaArgs;
 
 /*
@@ -155,6 +179,8 @@ typedef struct EkMixtralArgs {
                                    <0: next instruction's weights; 0 = off */
   int32_t record_timings;
   int64_t timeout_ns;
+  int32_t cache_flags;          /* EK_CACHE_* bits (the MLP prefetch bits apply to Llama only) */
+  int32_t prefetch_gap_ns;
 
   /* tensor parallel (after ek_tp_connect): this rank holds num_q_heads /
    * num_kv_heads / intermediate / vocab of its shard; `logits` must be the
@@ -209,7 +235,7 @@ int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* args, void* stream);
 
 /*
  * Tensor parallelism for Mixtral (no counterpart in the reference, whose
- * megakernel is single-GPU; SURVEY row e). Each rank calls ek_tp_setup, which
+ * megakernel is single-GPU). Each rank calls ek_tp_setup, which
  * allocates the rank's symmetric buffer (receive slots for the fp32 row
  * partials of O-proj and of the expert down projection, arrival counters, the
  * full-vocabulary logits) and returns its CUDA IPC handle (64 bytes) and the

@@ -35,12 +35,35 @@ def test_library_exports_all_declared_symbols():
     assert lib.ek_abi_version() == ek.EK_ABI_VERSION
 
 
-def test_struct_sizes_match_header():
-    # EkStatus: 8 int32; EkLlamaArgs: 23 pointers, 22 int32/float fields, padding, int64
-    assert ctypes.sizeof(ek.EkStatus) == 32
-    expect = 23 * 8 + 22 * 4
-    expect = (expect + 7) // 8 * 8 + 8
-    assert ctypes.sizeof(ek.EkLlamaArgs) == expect
+def _c_layout(struct: str, fields) -> dict:
+    """sizeof and offsetof of `struct` as the C compiler lays out include/ek.h."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = [f'printf("size %zu\\n", sizeof({struct}));']
+    lines += [f'printf("{f} %zu\\n", offsetof({struct}, {f}));' for f in fields]
+    src = ("#include <stddef.h>\n#include <stdio.h>\n#include \"ek.h\"\nint main(void) {\n"
+           + "\n".join(lines) + "\nreturn 0;\n}\n")
+    with tempfile.TemporaryDirectory() as d:
+        c, exe = Path(d) / "layout.c", Path(d) / "layout"
+        c.write_text(src)
+        subprocess.run([cc, "-I", str(HEADER.parent), "-o", str(exe), str(c)], check=True)
+        out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout
+    return {k: int(v) for k, v in (line.split() for line in out.splitlines())}
+
+
+@pytest.mark.parametrize("struct,cls", [("EkStatus", ek.EkStatus), ("EkLlamaArgs", ek.EkLlamaArgs),
+                                        ("EkMixtralArgs", ek.EkMixtralArgs)])
+def test_struct_layout_matches_header(struct, cls):
+    names = [n for n, _ in cls._fields_]
+    c = _c_layout(struct, names)
+    assert ctypes.sizeof(cls) == c["size"]
+    for n in names:
+        assert getattr(cls, n).offset == c[n], n
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path")
