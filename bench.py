@@ -3,8 +3,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--kv 2048] [--model 1b|3b|mixtral] [--prefetch S]
 
-A step is one decode token: embed, barrier reset, one megakernel launch over
-the whole model, argmax. The output token feeds the next step, as in
+A step is one decode token through `MK_Generator.run`: barrier reset and one
+megakernel launch over the whole model (for Llama the embedding gather and
+the argmax run inside the megakernel; Mixtral adds them as torch ops). The output token feeds the next step, as in
 MK_Generator.generate. Weights (2.47 GB) are far larger than L2 (126 MB), so
 no L2 flush is needed between steps.
 
@@ -298,7 +299,6 @@ def run_ours(args, rank, world, local):
     gen = MK_Generator(model, interp, sched)
     stream = torch.cuda.current_stream(dev)
     g = sched.globs
-    emb = model.model.embed_tokens.embed_tokens.weight
 
     tok = torch.zeros(1, 1, dtype=torch.long, device=dev)
     pos = args.kv
@@ -318,14 +318,9 @@ def run_ours(args, rank, world, local):
         with ClockSampler(local) as clocks:
             t_start.record(stream)
             for i in range(args.steps):
-                g.hidden_states[:] = emb[tok.view(-1)].view(-1)
-                gen.fill()
-                g.pos_id = pos
-                g.logits.zero_()
                 starts[i].record(stream)
-                interp.interpret(g)
+                tok = gen.run(tok, pos).view(1, 1)
                 ends[i].record(stream)
-                tok = torch.argmax(g.logits, dim=-1).view(1, 1)
                 kv_lens.append(pos + 1)
                 pos += 1
             t_end.record(stream)

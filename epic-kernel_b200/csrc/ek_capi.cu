@@ -362,7 +362,23 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   p.pf_gap_ns = a->prefetch_gap_ns > 0 ? (unsigned)a->prefetch_gap_ns : 0u;
   p.record = a->record_timings && a->timings ? 1 : 0;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 1000000000ll;
+  if (a->output_token && a->lm_head_instructions < 1)
+    return fail(EK_E_INVALID, "output_token needs lm_head_instructions >= 1");
+  if ((a->input_token == nullptr) != (a->embed_weights == nullptr))
+    return fail(EK_E_INVALID, "input_token and embed_weights go together");
+  if (a->embed_weights && !aligned16(a->embed_weights)) return fail(EK_E_INVALID, "embed_weights not 16-byte aligned");
+  p.in_token = reinterpret_cast<const long long*>(a->input_token);
+  p.embed = static_cast<const __nv_bfloat16*>(a->embed_weights);
+  p.out_token = reinterpret_cast<long long*>(a->output_token);
+  p.lm_count = a->lm_head_instructions;
   if (++ctx->epoch == 0) ctx->epoch = 1;
+  if (p.out_token && (ctx->epoch & 0xffffu) == 0) {
+    // the argmax key carries the epoch's low 16 bits: restart it at the wrap
+    cudaError_t e = cudaMemsetAsync(&ctx->status->argmax_key, 0, sizeof(unsigned long long),
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(argmax key)");
+    ++ctx->epoch;
+  }
   p.epoch = ctx->epoch;
 
   cudaError_t e = ek::launch_decode(p, static_cast<cudaStream_t>(stream));
@@ -447,7 +463,7 @@ extern "C" int ek_llama_decode_static(const EkLlamaArgs* a, void* stream, EkStat
     tmp.epoch = s.epoch;
     // the epoch tags every arrival counter with this call, so values left by
     // earlier calls are ignored; advance it here under the lock
-    if (++s.epoch == 0) s.epoch = 1;
+    do { ++s.epoch; } while (s.epoch == 0 || (s.epoch & 0xffffu) == 0);  // see the argmax key tag
     tmp.epoch = s.epoch - 1;  // ek_llama_decode pre-increments to s.epoch
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);

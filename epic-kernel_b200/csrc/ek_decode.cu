@@ -270,6 +270,19 @@ struct Consumer {
     return r;
   }
 
+  // The residual stream entering layer 0: hidden_states, or the embedding
+  // row of the input token (fused gather; a token outside the vocabulary is
+  // reported and row 0 used, so the launch drains without faulting).
+  __device__ __forceinline__ const __nv_bfloat16* layer0_input() const {
+    if (!p.in_token) return p.hidden;
+    long long t = __ldcg(p.in_token);
+    if (t < 0 || t >= p.V) {
+      if (tid == 0) record_error(p, 3, iidx, OP_QKV, 0, (int)t, p.V, -3);
+      t = 0;
+    }
+    return p.embed + (size_t)t * p.H;
+  }
+
   // Deferred down partials of layer `prev_layer` to add to the residual
   // stream (defer_down), or 0.
   __device__ __forceinline__ int deferred_splits(int prev_layer) const {
@@ -309,8 +322,8 @@ struct Consumer {
 
   // Residual-stream value of one row: hidden plus the nsplit deferred down
   // partials, in split order.
-  __device__ __forceinline__ float residual_value(int row, int nsplit) const {
-    float h = ldcg_bf16(p.hidden + row);
+  __device__ __forceinline__ float residual_value(const __nv_bfloat16* x, int row, int nsplit) const {
+    float h = ldcg_bf16(x + row);
     if (nsplit == 0) return h;
     const __nv_bfloat16* d = down_partials() + row;
     float parts[8];
@@ -430,7 +443,8 @@ struct Consumer {
       return;
     }
     stamp(1);
-    rmsnorm_to_act(p.hidden, p.attn_ln + (size_t)l * p.H, p.H, nw, deferred_splits(l - 1));
+    rmsnorm_to_act(l == 0 ? layer0_input() : p.hidden, p.attn_ln + (size_t)l * p.H, p.H, nw,
+                   deferred_splits(l - 1));
     stamp(3);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
@@ -781,6 +795,7 @@ struct Consumer {
     // attention wait, so that its latency overlaps the wait
     const bool own_rows = o && splits == 1 && p.tp_world <= 1;
     const int nsplit = own_rows ? deferred_splits(l - 1) : 0;
+    const __nv_bfloat16* xres = l == 0 ? layer0_input() : p.hidden;
     float hpre = 0.f;
     if (own_rows) {
       if (nsplit > 0) {
@@ -788,7 +803,7 @@ struct Consumer {
         const int t = p.down_done_target;
         if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
       }
-      if (tid < nrows) hpre = residual_value(b0 * 16 + tid, nsplit);
+      if (tid < nrows) hpre = residual_value(xres, b0 * 16 + tid, nsplit);
     }
     {
       int* a = o ? bar(l, OP_REDUCTION - 1, 0) : bar(l, OP_UPGATE - 1, 0);
@@ -832,7 +847,7 @@ struct Consumer {
       const int row = (b0 + j) * 16 + r;
       const float v = bf16r(row_sum(part, j * spb, R, r));
       if (splits == 1) {
-        const float h = own_rows && idx == tid ? hpre : residual_value(row, nsplit);
+        const float h = own_rows && idx == tid ? hpre : residual_value(xres, row, nsplit);
         p.hidden[row] = __float2bfloat16_rn(h + v);
       } else {
         partials[(size_t)split * p.H + row] = __float2bfloat16_rn(v);
@@ -913,10 +928,55 @@ struct Consumer {
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
     stamp(4);
+    unsigned long long best = 0;  // argmax key of this thread's rows
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
-      p.logits[(b0 + j) * 16 + r] = __float2bfloat16_rn(row_sum(part, j * spb, p.H, r));
+      const __nv_bfloat16 v = __float2bfloat16_rn(row_sum(part, j * spb, p.H, r));
+      p.logits[(b0 + j) * 16 + r] = v;
+      best = max(best, argmax_key(v, (b0 + j) * 16 + r));
     }
+    if (p.out_token) finish_argmax(best);
+  }
+
+  // Argmax key: launch tag, bf16 value mapped to an unsigned order, then the
+  // row complemented, so that the largest key is the largest value's first row
+  // (torch.argmax's tie rule).
+  __device__ __forceinline__ unsigned long long argmax_key(__nv_bfloat16 v, int row) const {
+    unsigned b = __bfloat16_as_ushort(v);
+    b = (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+    return ((unsigned long long)(p.epoch & 0xffffu) << 48) | ((unsigned long long)b << 32) |
+           (unsigned long long)(0xffffffffu - (unsigned)row);
+  }
+
+  // Merge this instruction's best key into the launch's, count the
+  // instruction, and let the last LM-head instruction write the token.
+  __device__ void finish_argmax(unsigned long long best) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    // CW keys in the activation area (the GEMV that read it has finished)
+    unsigned long long* wbest = reinterpret_cast<unsigned long long*>(act);
+    if (lane == 0) wbest[warp] = best;
+    sync();
+    if (tid == 0) {
+      for (int w = 0; w < CW; ++w) best = max(best, wbest[w]);
+      atomicMax(&p.status->argmax_key, best);
+      __threadfence();
+      // epoch-tagged arrival count (a count left by an earlier launch restarts)
+      const unsigned long long tag = (unsigned long long)p.epoch << 32;
+      unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(&p.status->lm_arrivals), nv;
+      while (true) {
+        nv = ((old & ~0xffffffffull) == tag) ? old + 1 : (tag | 1ull);
+        const unsigned long long prev = atomicCAS(&p.status->lm_arrivals, old, nv);
+        if (prev == old) break;
+        old = prev;
+      }
+      if ((int)(nv & 0xffffffffull) == p.lm_count) {
+        __threadfence();
+        const unsigned long long k = atomicMax(&p.status->argmax_key, 0ull);
+        *p.out_token = (long long)(0xffffffffu - (unsigned)(k & 0xffffffffull));
+      }
+    }
+    sync();
   }
   // ---------------------------------------------------------------- tensor parallel
   __device__ __forceinline__ float* tp_slot(int rank, long long off) const {

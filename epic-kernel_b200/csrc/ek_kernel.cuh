@@ -100,8 +100,15 @@ enum Model : int { MODEL_LLAMA = 0, MODEL_MIXTRAL = 1 };
 struct DevStatus {
   int code, sm, instr, opcode, layer, observed, expected, detail;
   unsigned abort_epoch;  // == current epoch once any block failed in this launch
-  int pad[7];
+  int pad0;
+  // fused argmax of the logits (Llama, output_token set): the best
+  // (epoch16, ordered bf16 value, ~row) key of the launch, and the LM-head
+  // instructions finished in it (epoch << 32 | count)
+  unsigned long long argmax_key;
+  unsigned long long lm_arrivals;
+  int pad[2];
 };
+static_assert(sizeof(DevStatus) == 64, "status record");
 
 struct KParams {
   CUtensorMap tm_k, tm_v;  // KV caches [L*T, Hkv, D], box D x 1 x tk
@@ -185,6 +192,14 @@ struct KParams {
   // AttentionReduction; the reduction instructions become no-ops. Only for
   // schedules whose reductions are terminal over all partials in order.
   int fuse_red;
+  // fused embedding gather and argmax (Llama): layer 0 reads the residual
+  // stream from embed[*in_token] instead of `hidden`; the LM head writes the
+  // first index of the largest logit to *out_token once all lm_count LM-head
+  // instructions finished
+  const long long* in_token;
+  const __nv_bfloat16* embed;
+  long long* out_token;
+  int lm_count;
   long long timeout_ns;
   unsigned epoch;
 };

@@ -59,9 +59,21 @@ def _stream_options(globs, options):
 class LatencyMK_Interpreter(MK_Interpreter):
     """`options` are passed to every launch (e.g. l2_prefetch_stages)."""
 
+    supports_fused_step = True
+
     def __init__(self, mk_dir: Path | str | None = None, **options):
         super().__init__(mk_dir)
         self.options = options
+
+    def interpret_step(self, globs: Globals, input_token, embed_weights, output_token):
+        """One decode step with the embedding gather and the argmax done inside
+        the megakernel (no extra launches): layer 0 reads
+        embed_weights[input_token], and the argmax of the logits lands in
+        output_token (int64 device tensors)."""
+        n_lm = getattr(globs, "lm_head_instructions", 0)
+        interpret_with_mk(globs, self.mk_func, input_token=input_token, embed_weights=embed_weights,
+                          output_token=output_token, lm_head_instructions=n_lm,
+                          **_stream_options(globs, self.options))
 
     def interpret(self, globs: Globals):
         interpret_with_mk(globs, self.mk_func, **_stream_options(globs, self.options))

@@ -68,6 +68,7 @@ class EkLlamaArgs(ctypes.Structure):
         ("timeout_ns", ctypes.c_int64),
         ("cache_flags", _I), ("prefetch_gap_ns", _I),
         ("options", _I), ("deferred_down_layers", _I),
+        ("input_token", _P), ("embed_weights", _P), ("output_token", _P), ("lm_head_instructions", _I),
     ]
 
 

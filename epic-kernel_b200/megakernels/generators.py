@@ -4,7 +4,9 @@ epic-kernel, :11-166).
 `MK_Generator.run` does per token what the reference does: embed the input
 token into `hidden_states`, reset the barrier counters, zero the logits, launch
 the megakernel, and take the argmax of the logits, all on the current stream
-with no host synchronisation.
+with no host synchronisation. With an interpreter that supports the fused
+step (the Llama engine), the gather and the argmax run inside the megakernel
+and a step is one barrier reset plus one launch.
 """
 
 import torch
@@ -46,6 +48,16 @@ class MK_Generator(Generator):
         self.skip_rest = skip_rest
         self.fill()
 
+    def _fused_step(self) -> bool:
+        if self.skip_mk or self.skip_rest or not getattr(self.interpreter, "supports_fused_step", False):
+            return False
+        if getattr(self.schedule.globs, "lm_head_instructions", 0) < 1:
+            return False
+        if not hasattr(self, "_tokens"):
+            self._tokens = torch.zeros(2, 1, dtype=torch.int64, device=self.schedule.globs.hidden_states.device)
+            self._flip = 0
+        return True
+
     def fill(self):
         self.schedule.globs.barriers.fill_(self.barrier_fill_val)
 
@@ -54,6 +66,19 @@ class MK_Generator(Generator):
 
     def run(self, input_ids: Tensor, pos_id: int) -> Tensor:
         globs = self.schedule.globs
+        if self._fused_step():
+            # embedding gather and argmax inside the megakernel; the output
+            # token alternates between two buffers so that a step may read the
+            # previous step's token while writing its own
+            self.fill()
+            globs.pos_id = pos_id
+            out = self._tokens[self._flip]
+            self._flip ^= 1
+            ids = input_ids.reshape(-1)[:1]
+            if ids.dtype != torch.int64:
+                ids = ids.to(torch.int64)
+            self.interpreter.interpret_step(globs, ids, self.model.model.embed_tokens.embed_tokens.weight, out)
+            return out[0]
         if not self.skip_rest:
             emb = self.model.model.embed_tokens(BatchState(input_ids=input_ids))
             globs.hidden_states[:] = emb.hidden_states.reshape(-1)

@@ -35,6 +35,12 @@ Extra keyword-only options (defaults match the reference's behaviour):
                       column-split partials for layer l + 1 to add (the
                       interpreter passes what `tensorize_instructions` found
                       safe for the stream)
+  input_token, embed_weights, output_token, lm_head_instructions
+                      fused token step: layer 0 reads embed_weights[input_token]
+                      (int64 device scalar) instead of hidden_states, and the
+                      argmax of the logits (first index on ties) is written to
+                      output_token (int64); lm_head_instructions = number of
+                      RMS_LM_Head instructions in the queues
 
 Errors: bad shapes or dtypes raise ValueError before launch; a CUDA launch
 failure raises RuntimeError. Device-side failures (timeouts, malformed
@@ -169,6 +175,7 @@ def mk_llama(
     timeout_ns: int = 0, down_reduction_size: int = 0,
     cache_flags: int | None = None, prefetch_gap_ns: int = 0, fuse_attention_reduction: bool = False,
     deferred_down_layers: int = 0,
+    input_token=None, embed_weights=None, output_token=None, lm_head_instructions: int = 0,
 ):
     tensors = (barriers, instructions, timings, qkv_proj_weights, attn_ln_weights, o_proj_weights,
                mlp_ln_weights, up_proj_weights, gate_proj_weights, down_proj_weights,
@@ -193,6 +200,13 @@ def mk_llama(
     args.attn_scale = float(attn_scale)
     args.rms_norm_eps = float(rms_norm_eps)
     args.skip_attn_reduction = int(bool(skip_attn_reduction))
+    # fused token step: per-call device pointers (int64 token ids, embedding table)
+    if (input_token is None) != (embed_weights is None):
+        raise ValueError("mk_llama: input_token and embed_weights go together")
+    args.input_token = _need(input_token, "input_token", torch.int64) if input_token is not None else None
+    args.embed_weights = _need(embed_weights, "embed_weights", _BF16, 2) if embed_weights is not None else None
+    args.output_token = _need(output_token, "output_token", torch.int64) if output_token is not None else None
+    args.lm_head_instructions = int(lm_head_instructions)
     ctx = ek.context_for(device)
     if stream is None:
         stream = torch.cuda.current_stream(device)

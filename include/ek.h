@@ -127,6 +127,16 @@ typedef struct EkLlamaArgs {
    * stream (same order and rounding as adding them at once). The instruction
    * stream must then hold layer l + 1's QKV and O-proj instructions; 0 = off. */
   int32_t deferred_down_layers;
+  /* Fused token step (all optional, NULL = off). With input_token (int64, one
+   * token id) and embed_weights ([vocab, H] bf16), layer 0 reads the token's
+   * embedding row instead of hidden_states (which the step then overwrites).
+   * With output_token (int64), the index of the largest logit (the first one
+   * on ties, as torch.argmax) is written there; lm_head_instructions must then
+   * be the number of RMS_LM_Head instructions in the queues. */
+  const int64_t* input_token;
+  const void* embed_weights;
+  int64_t* output_token;
+  int32_t lm_head_instructions;
 } EkLlamaArgs;
 
 /*
