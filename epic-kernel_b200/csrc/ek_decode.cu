@@ -84,8 +84,11 @@ __device__ __noinline__ uint2 gemv_blocks_rps(const KParams& p, const uint8_t* s
     for (int rg = 0; rg < 16 / RPS; ++rg) {
       for (int c = 0; c < nch; ++c, ++k) {
         stage_wait(p, &full[slot], parity, ring_timeout, broken, iidx, (int)slot);
-        if (timing != 0xffffffffu && tid == 0 && k < 28)
-          p.timings[(size_t)timing * 128 + 8 + k] = (int)(globaltimer() & 0x7fffffff);
+        if (timing != 0xffffffffu && tid == 0 && k < 28) {
+          const int now = (int)(globaltimer() & 0x7fffffff);
+          p.timings[(size_t)timing * 128 + TS_STAGE_USE + k] = now;
+          if (k == 0) p.timings[(size_t)timing * 128 + TS_FIRST_USE] = now;
+        }
         const uint4* w4 = reinterpret_cast<const uint4*>(stages + (size_t)slot * STAGE_BYTES);
         const int x0 = c * (STAGE_BYTES / 2);
         const int npieces = FULL ? 1024 : RPS * (min(STAGE_BYTES / 2, S - x0) / 8);
@@ -216,6 +219,7 @@ struct Consumer {
   // by p.timeout_ns. Returns (to all consumer threads) whether to run the op.
   __device__ bool wait_counters(int n, int* const* addrs, const int* targets, int opcode, int layer,
                                 bool sys_scope = false) {
+    if (n > 0) stamp(TS_WAIT);
     if (tid == 0) {
       int ok = 1;
       for (int j = 0; j < n && ok; ++j) {
@@ -253,8 +257,12 @@ struct Consumer {
   }
 
   __device__ __forceinline__ void stamp(int slot) {
-    if (p.record && tid == 0 && p.timings)
-      p.timings[((size_t)qidx * p.Q + iidx) * 128 + slot] = (int)(globaltimer() & 0x7fffffff);
+    if (p.record && tid == 0 && p.timings) {
+      int* t = p.timings + ((size_t)qidx * p.Q + iidx) * 128;
+      const int now = (int)(globaltimer() & 0x7fffffff);
+      t[slot] = now;
+      if (slot == TS_STORE) t[TS_LAST_USE] = now;  // the GEMV stages end where the epilogue begins
+    }
   }
 
   // Norm weights a thread needs (its pieces c = tid, tid + NC), loaded before
@@ -442,14 +450,14 @@ struct Consumer {
       drain(pl.ns);
       return;
     }
-    stamp(1);
+    stamp(TS_READY);
     rmsnorm_to_act(l == 0 ? layer0_input() : p.hidden, p.attn_ln + (size_t)l * p.H, p.H, nw,
                    deferred_splits(l - 1));
-    stamp(3);
+    stamp(TS_ACT);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
-    stamp(4);
+    stamp(TS_STORE);
     // one thread per rotary pair (rows 2i, 2i + 1 of a block)
 #pragma unroll 1
     for (int idx = tid; idx < (b1 - b0) * 8; idx += NC) {
@@ -587,7 +595,7 @@ struct Consumer {
       t[gqa] = t[gqa + 1] = bph;
       if (!wait_counters(gqa + 2, a, t, OP_PARTIAL, l)) { drain(pl.ns); return; }
     }
-    stamp(1);
+    stamp(TS_READY);
     const TokenRange tr = partial_tokens(p, P, part);
     // this lane's q chunks (score role), rotated like the K reads
     uint4 qr[R::NQ];
@@ -599,7 +607,7 @@ struct Consumer {
 #pragma unroll
       for (int i = 0; i < R::NQ; ++i) qr[i] = __ldcg(q4 + (i + rot) % R::NQ);
     }
-    stamp(3);
+    stamp(TS_ACT);
     float ms = -INFINITY, ls = 0.f, acc[R::VD];
 #pragma unroll
     for (int e = 0; e < R::VD; ++e) acc[e] = 0.f;
@@ -618,7 +626,7 @@ struct Consumer {
       attend_tile<D>(reinterpret_cast<const uint8_t*>(p.k_cache + off),
                      reinterpret_cast<const uint8_t*>(p.v_cache + off), 1, true, qr, ms, ls, acc, gqa);
     }
-    stamp(4);
+    stamp(TS_STORE);
     // merge the per-warp online-softmax states
     float* mm = reinterpret_cast<float*>(act);  // [CW][gqa]
     float* ll = mm + CW * MAX_GQA;              // [CW][gqa]
@@ -695,7 +703,7 @@ struct Consumer {
       int* a = bar(l, OP_PARTIAL - 1, hs);
       if (!wait_counters(1, &a, &P, OP_REDUCTION, l)) return;
     }
-    stamp(1);
+    stamp(TS_READY);
     merge_partials(l, hs, n, ins.w + 6, terminal != 0, ins.w[6 + n]);
   }
 
@@ -810,15 +818,15 @@ struct Consumer {
       const int t = o ? p.Hq : p.I / 16;
       if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
     }
-    stamp(1);
+    stamp(TS_READY);
     copy_to_act((o ? p.attn_out : p.silu) + (size_t)split * R, R);
-    stamp(3);
+    stamp(TS_ACT);
     // partial sums: [o_splits][H] for O_ProjResidual, then [down_splits][H]
     __nv_bfloat16* partials = p.split_partials + (size_t)(o ? 0 : p.o_splits) * p.H;
     const int spb = stages_per_row_block(R);
     float* part = partials_after(R);
     gemv_stream(pl.ns, R, part);
-    stamp(4);
+    stamp(TS_STORE);
     if (kMixtral && o && p.tp_world > 1) {
       // tensor parallel: all-reduce the fp32 row partials over NVLink, then
       // add their rank-ordered sum, rounded once, to hidden (same on all ranks)
@@ -894,13 +902,13 @@ struct Consumer {
       const int t = p.H / 16;
       if (!wait_counters(1, &a, &t, OP_UPGATE, l)) { drain(pl.ns); return; }
     }
-    stamp(1);
+    stamp(TS_READY);
     rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H, nw);
-    stamp(3);
+    stamp(TS_ACT);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
-    stamp(4);
+    stamp(TS_STORE);
     for (int idx = tid; idx < n * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
       const float u = bf16r(row_sum(part, j * 2 * spb, p.H, r));
@@ -921,13 +929,13 @@ struct Consumer {
       const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
     }
-    stamp(1);
+    stamp(TS_READY);
     rmsnorm_to_act(p.hidden, p.lm_norm, p.H, nw);
-    stamp(3);
+    stamp(TS_ACT);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
-    stamp(4);
+    stamp(TS_STORE);
     unsigned long long best = 0;  // argmax key of this thread's rows
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
       const int j = idx / 16, r = idx % 16;
@@ -1077,7 +1085,7 @@ struct Consumer {
         return;
       }
     }
-    stamp(1);
+    stamp(TS_READY);
     rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H, nw);
     router(l);
     if (pl.ns > 0) handoff(rsel);
@@ -1089,11 +1097,11 @@ struct Consumer {
       const uint4* xs = reinterpret_cast<const uint4*>(act);
       for (int c = tid; c < p.H / 8; c += NC) reinterpret_cast<uint4*>(p.router_normed)[c] = xs[c];
     }
-    stamp(3);
+    stamp(TS_ACT);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
-    stamp(4);
+    stamp(TS_STORE);
     for (int idx = tid; idx < p.topk * nb * 16; idx += NC) {
       const int es = idx / (nb * 16), j = (idx / 16) % nb, r = idx % 16;
       const int first = (es * nb + j) * 2 * spb;
@@ -1120,7 +1128,7 @@ struct Consumer {
         return;
       }
     }
-    stamp(1);
+    stamp(TS_READY);
     if (tid < p.topk) {
       int e = __ldcg(p.sel_idx + tid);
       rsel[tid] = (e < 0 || e >= p.E) ? 0 : e;
@@ -1135,7 +1143,7 @@ struct Consumer {
       copy_to_act(p.expert_silu + (size_t)rsel[es] * p.I, p.I);
       gemv_stream(nse, p.I, part + es * nb * BLOCK_PART);
     }
-    stamp(4);
+    stamp(TS_STORE);
     if (p.tp_world > 1) {
       // tensor parallel: all-reduce each expert's fp32 row partials
       for (int idx = tid; idx < p.topk * nb * 16; idx += NC) {
@@ -1185,13 +1193,13 @@ struct Consumer {
       const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_LM_HEAD, p.L - 1)) { drain(pl.ns); return; }
     }
-    stamp(1);
+    stamp(TS_READY);
     rmsnorm_to_act(p.hidden, p.lm_norm, p.H, nw);
-    stamp(3);
+    stamp(TS_ACT);
     const int spb = stages_per_row_block(LM_HEAD_SPLIT);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, LM_HEAD_SPLIT, part, split * LM_HEAD_SPLIT);
-    stamp(4);
+    stamp(TS_STORE);
     if (p.tp_world > 1) {
       // tensor parallel: this rank's vocabulary rows go into every rank's logits
       for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
@@ -1225,7 +1233,7 @@ struct Consumer {
     } else if (!wait_counters(0, nullptr, nullptr, OP_PREDICT, l)) {
       return;
     }
-    stamp(1);
+    stamp(TS_READY);
     rmsnorm_to_act(p.hidden, p.ffn_ln + (size_t)l * p.H, p.H, nw);
     router(l);
     if (tid < p.topk) p.pred_idx[tid] = rsel[tid];
@@ -1441,8 +1449,8 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
               return;
             }
           }
-          if (p.record && p.timings && wk.k + t < 56)
-            p.timings[((size_t)q * p.Q + i) * 128 + 64 + wk.k + t] = (int)(globaltimer() & 0x7fffffff);
+          if (p.record && p.timings && wk.k + t < 16)
+            p.timings[((size_t)q * p.Q + i) * 128 + TS_STAGE_LOAD + wk.k + t] = (int)(globaltimer() & 0x7fffffff);
           uint64_t* fb = &ring.full[ring.slot];
           uint8_t* dst = ring.stages + (size_t)ring.slot * STAGE_BYTES;
           mbar_arrive_expect_tx(fb, rr.bytes * (uint32_t)rr.copies);
@@ -1469,8 +1477,8 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
           return;
         }
       }
-      if (p.record && p.timings && wk.k < 56)
-        p.timings[((size_t)q * p.Q + i) * 128 + 64 + wk.k] = (int)(globaltimer() & 0x7fffffff);
+      if (p.record && p.timings && wk.k < 16)
+        p.timings[((size_t)q * p.Q + i) * 128 + TS_STAGE_LOAD + wk.k] = (int)(globaltimer() & 0x7fffffff);
       wk.issue<false>(p, ring.stages + (size_t)ring.slot * STAGE_BYTES, &ring.full[ring.slot]);
       ring_advance(ring);
       ++g_load;
@@ -1478,8 +1486,8 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
   }
   // diagnostics: stages loaded and prefetched by this queue's loader
   if (p.record && p.timings) {
-    p.timings[(size_t)q * p.Q * 128 + 126] = pf.issued;
-    p.timings[(size_t)q * p.Q * 128 + 127] = (int)g_load;
+    p.timings[(size_t)q * p.Q * 128 + TS_DIAG] = pf.issued;
+    p.timings[(size_t)q * p.Q * 128 + TS_DIAG + 1] = (int)g_load;
   }
 }
 
@@ -1554,7 +1562,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     if (tid < 32) ins.w[tid] = __ldg(p.instructions + ((size_t)blockIdx.x * p.Q + i) * 32 + tid);
     c.sync();
     const Plan pl = make_plan(p, ins);
-    c.stamp(0);
+    c.stamp(TS_START);
     if (pl.bad_word >= 0) {
       if (tid == 0)
         record_error(p, pl.bad_word == 0 && (pl.op < 0 || pl.op > (kMixtral ? OP_PREDICT : OP_LM_HEAD)) ? 2 : 3, i, pl.op,
@@ -1570,7 +1578,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
         case OP_PREDICT: c.op_predict(ins); break;
         default: break;
       }
-      c.stamp(2);
+      c.stamp(TS_END);
       c.sync();
       continue;
     }
@@ -1585,7 +1593,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
       case OP_LM_HEAD: c.op_lm_head(ins, pl); break;
       default: break;
     }
-    c.stamp(2);
+    c.stamp(TS_END);
     c.sync();  // act / red / flag are reused by the next instruction
   }
   // tensor parallel: the logits are complete once every rank's LM-head

@@ -85,6 +85,22 @@ enum Op : int {
   OP_PREDICT = 8,  // Mixtral SpeculativeExpertPredict
 };
 
+// Slots of timings[queue][instruction][128] (globaltimer ns, low 31 bits),
+// following the reference's TEVENT convention (include/util.cuh:221-245 of
+// epic-kernel) so that its timing plots read them.
+constexpr int TS_START = 0;        // TEVENT_CONTROLLER_START: instruction begins
+constexpr int TS_END = 4;          // TEVENT_CONTROLLER_END: instruction done
+constexpr int TS_WAIT = 44;        // TEVENT_AT_GMEM_WAIT: counter wait begins
+constexpr int TS_READY = 45;       // TEVENT_DONE_GMEM_WAIT: dependencies satisfied
+constexpr int TS_STORE = 46;       // TEVENT_AT_GMEM_STORE: epilogue (results, counters) begins
+constexpr int TS_FIRST_USE = 49;   // TEVENT_FIRST_USE: first ring stage acquired
+constexpr int TS_LAST_USE = 52;    // TEVENT_LAST_USE: last ring stage consumed
+constexpr int TS_ACT = 55;         // activation vector staged in shared memory (free slot)
+constexpr int TS_STAGE_USE = 56;   // + k (k < 28): consumers acquired ring stage k
+constexpr int TS_STAGE_LOAD = 84;  // + k (k < 16): loader issued ring stage k
+constexpr int TS_PREFETCH = 100;   // 100 / 101: MLP prefetcher start / end (prefetch variant)
+constexpr int TS_DIAG = 126;       // instruction 0 only: 126 prefetched stages, 127 loaded stages
+
 enum CacheBits : int {
   PF_UPGATE = 1,
   PF_DOWN = 2,

@@ -141,6 +141,14 @@ def test_timings_recorded(tiny_gpu):
     pos = 5
     s = prepare(tiny_gpu, pos, cases.step_hidden(2048, pos))
     run_gpu(s, record_timings=True)
-    t = s.globs.timings
+    t = s.globs.timings.long()
     real = s.globs.instructions[:, :, 0] != 0
-    assert bool((t[:, :, 2][real] != 0).all())
+    # the reference's TEVENT slots: 0 controller start, 4 controller end,
+    # 44 / 45 around the cross-SM wait (include/util.cuh:221-245 of epic-kernel)
+    start, end = t[:, :, 0][real], t[:, :, 4][real]
+    assert bool((start != 0).all()) and bool((end != 0).all())
+    assert bool((end >= start).all())
+    waited = real & (t[:, :, 44] != 0)
+    assert bool(waited.any())
+    assert bool((t[:, :, 45][waited] >= t[:, :, 44][waited]).all())
+    assert bool((t[:, :, 45][waited] <= t[:, :, 4][waited]).all())
