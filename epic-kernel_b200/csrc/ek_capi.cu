@@ -586,6 +586,7 @@ extern "C" int ek_mixtral_decode(EkContext* ctx, const EkMixtralArgs* a, void* s
   p.scale = a->attn_scale; p.eps = a->rms_norm_eps;
   p.down_R = I; p.o_R = Hq * D; p.down_splits = 1; p.o_splits = 1;
   p.tp_world = 1;
+  p.spec_stages = a->speculative_prefetch_stages > 0 ? a->speculative_prefetch_stages : 0;
   if (tp) {
     p.tp_world = ctx->tp_world;
     p.tp_rank = ctx->tp_rank;

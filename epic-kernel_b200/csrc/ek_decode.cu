@@ -1388,6 +1388,30 @@ __device__ void run_mlp_prefetcher(const KParams& p) {
   }
 }
 
+// Mixtral RmsRouterUpgate: before the loader waits for the router's choice,
+// L2-prefetch the first spec_stages ring stages of each predicted expert
+// (SpeculativeExpertPredict's output for this layer, awaited with a short
+// bound; a late or wrong guess only wastes the prefetch), as the reference's
+// loader does (demos/mixtral/rms_router_matvec.cu:258-289).
+__device__ void speculative_prefetch(const KParams& p, const Ins& ins, const Plan& pl) {
+  const int* c = p.barriers + ((size_t)pl.layer * p.brow + (OP_PREDICT - 1)) * p.bcol;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire(c) < 1) {
+    if (aborted(p) || (long long)(globaltimer() - t0) > p.timeout_ns) return;
+    __nanosleep(64);
+  }
+  int pred[MAX_TOPK];
+  for (int t = 0; t < MAX_TOPK; ++t) pred[t] = t < p.topk ? ld_relaxed(p.pred_idx + t) : 0;
+  const int per_expert = min(p.spec_stages, pl.ns / p.topk);
+  for (int e = 0; e < p.topk; ++e) {
+    int rot[MAX_TOPK];
+    for (int t = 0; t < MAX_TOPK; ++t) rot[t] = pred[(e + t) % p.topk];
+    StageWalker w;
+    w.init(p, ins, pl, rot);
+    for (int k = 0; k < per_expert && !w.done(); ++k) w.issue<true>(p, nullptr, nullptr);
+  }
+}
+
 // lins / pins: shared-memory instruction buffers of the loader and of its L2
 // prefetch cursor (dynamically indexed words stay out of local memory).
 __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_t* mbox_bar, Ins* lins,
@@ -1412,6 +1436,7 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
       // which experts to stream is decided by the consumers (router, or the
       // router outputs of another SM): wait for their handoff, prefetching
       // ahead into L2 meanwhile
+      if (pl.op == OP_UPGATE && p.spec_stages > 0) speculative_prefetch(p, ins, pl);
       while (kPrefetch && p.pf_stages > 0 && pf.g < g_load + p.pf_stages && !mbar_test_wait(mbox_bar, mbox_phase))
         if (!pf.step(p, q, g_load)) break;
       if (!ring_wait(mbox_bar, mbox_phase, ring_timeout)) {

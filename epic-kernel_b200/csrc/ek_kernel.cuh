@@ -216,6 +216,7 @@ struct KParams {
   const __nv_bfloat16* embed;
   long long* out_token;
   int lm_count;
+  int spec_stages;  // Mixtral: stages per predicted expert L2-prefetched before the router handoff
   long long timeout_ns;
   unsigned epoch;
 };

@@ -94,7 +94,7 @@ class EkMixtralArgs(ctypes.Structure):
         ("l2_prefetch_stages", _I), ("record_timings", _I),
         ("timeout_ns", ctypes.c_int64),
         ("cache_flags", _I), ("prefetch_gap_ns", _I),
-        ("tp_lm_instructions", _I),
+        ("tp_lm_instructions", _I), ("speculative_prefetch_stages", _I),
     ]
 
 

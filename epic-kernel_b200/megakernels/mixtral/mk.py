@@ -60,4 +60,18 @@ class MixtralMK_Interpreter(MK_Interpreter):
         self.options = options
 
     def interpret(self, globs: MixtralGlobals):
-        interpret_with_mk(globs, self.mk_func, **self.options)
+        interpret_with_mk(globs, self.mk_func, **stream_options(globs, self.options))
+
+
+# ring stages per predicted expert prefetched into L2 before the router's choice
+SPECULATIVE_PREFETCH_STAGES = 16
+
+
+def stream_options(globs, options):
+    """Engine options that depend on the instruction stream: the speculative
+    expert prefetch runs only when the queues hold SpeculativeExpertPredict
+    instructions (as `tensorize_instructions` recorded)."""
+    opts = dict(options)
+    opts.setdefault("speculative_prefetch_stages",
+                    SPECULATIVE_PREFETCH_STAGES if getattr(globs, "expert_predictions", 0) else 0)
+    return opts

@@ -171,7 +171,8 @@ def make_dag_layer(globs: MixtralGlobals, layer_idx: int, prev: list[DAG_Node], 
     qkv = [DAG_Node(ins, prev) for ins in schedule_qkv(globs, layer_idx)]
     owner = {b: n for n in qkv for b in n.instruction.block_indices()}
     new.extend(qkv)
-    new.extend(DAG_Node(ins, prev) for ins in schedule_speculative_predict(globs, layer_idx))
+    if getattr(globs, "speculative_prediction", True):
+        new.extend(DAG_Node(ins, prev) for ins in schedule_speculative_predict(globs, layer_idx))
     if stop_after_op == "qkv":
         return new, qkv
 
@@ -227,3 +228,15 @@ class MixtralLatencyScheduleBuilder(ScheduleBuilder):
     @classmethod
     def make_dag(cls, globs, stop_after_op=None, layer_limit=None):
         return make_dag(globs, stop_after_op, layer_limit)
+
+
+class MixtralNoSpeculationScheduleBuilder(MixtralLatencyScheduleBuilder):
+    """The same schedule without SpeculativeExpertPredict instructions (the
+    "speculative prediction off" configuration); the engine then prefetches
+    no expert weights before the router's choice."""
+
+    @classmethod
+    def make_globals(cls, model, seq_len: int = 0) -> MixtralGlobals:
+        globs = make_globals(model, seq_len=seq_len)
+        globs.speculative_prediction = False
+        return globs

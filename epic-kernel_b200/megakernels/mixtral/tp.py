@@ -81,6 +81,7 @@ class MixtralTPMK_Interpreter(MixtralMK_Interpreter):
     def interpret(self, globs):
         if not hasattr(globs, "_tp_lm_count"):
             globs._tp_lm_count = lm_head_instruction_count(globs)
-        from megakernels.mixtral.mk import interpret_with_mk
+        from megakernels.mixtral.mk import interpret_with_mk, stream_options
 
-        interpret_with_mk(globs, self.mk_func, tp_lm_instructions=globs._tp_lm_count, **self.options)
+        interpret_with_mk(globs, self.mk_func, tp_lm_instructions=globs._tp_lm_count,
+                          **stream_options(globs, self.options))

@@ -235,6 +235,8 @@ def tensorize_instructions(globs: BaseGlobals, instruction_queues: list[list[Ins
     globs.attention_reduction_fusable = attention_reduction_fusable(globs, instruction_queues)
     globs.deferrable_down_layers = deferrable_down_layers(instruction_queues)
     globs.lm_head_instructions = sum(1 for q in instruction_queues for ins in q if ins.opcode() == 7)
+    globs.expert_predictions = sum(
+        1 for q in instruction_queues for ins in q if type(ins).__name__ == "SpeculativeExpertPredict")
     words = [serialize_and_pad(ins) for q in instruction_queues for ins in q]
     globs.instructions = torch.tensor(words, dtype=torch.int32).view(
         num_sms, queue_len, INTS_PER_INSTRUCTION

@@ -8,7 +8,9 @@ weights flattened to [L * E, ...], router [L * E, H], FFN norms, LM head
 outputs, then pos_id, attn_scale, rms_norm_eps, skip_attn_reduction, and
 `stream=`. Keyword-only options: l2_prefetch_stages (lookahead L2 prefetch,
 which also prefetches the predicted experts of expert instructions),
-record_timings, timeout_ns, tp_lm_instructions (tensor parallel: LM-head
+record_timings, timeout_ns, speculative_prefetch_stages (ring stages per
+predicted expert L2-prefetched before the router's choice; 0 = off),
+tp_lm_instructions (tensor parallel: LM-head
 instructions per rank, set by megakernels.mixtral.tp).
 """
 
@@ -107,6 +109,7 @@ def mk_mixtral(
     pos_id, attn_scale, rms_norm_eps, skip_attn_reduction,
     *, stream=None, l2_prefetch_stages: int = 0, record_timings: bool = False, timeout_ns: int = 0,
     tp_lm_instructions: int = 0, cache_flags: int | None = None, prefetch_gap_ns: int = 0,
+    speculative_prefetch_stages: int = 0,
 ):
     t = (barriers, instructions, timings, qkv_weights, attn_norm_weights, o_weights, expert_gate_weights,
          expert_up_weights, expert_down_weights, router_weights, ffn_ln_weights, lm_head_norm_weights,
@@ -130,6 +133,7 @@ def mk_mixtral(
     args.attn_scale = float(attn_scale)
     args.rms_norm_eps = float(rms_norm_eps)
     args.skip_attn_reduction = int(bool(skip_attn_reduction))
+    args.speculative_prefetch_stages = int(speculative_prefetch_stages)
     ctx = ek.context_for(device)
     if stream is None:
         stream = torch.cuda.current_stream(device)

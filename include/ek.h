@@ -196,6 +196,11 @@ typedef struct EkMixtralArgs {
    * num_kv_heads / intermediate / vocab of its shard; `logits` must be the
    * context's symmetric logits buffer (full vocabulary, vocab * world rows). */
   int32_t tp_lm_instructions;   /* Mixtral_RMS_LM_Head instructions in this rank's queues */
+  /* Ring stages (16 KiB) per predicted expert that RmsRouterUpgate's loader
+   * prefetches into L2 before the router's choice arrives, once this layer's
+   * SpeculativeExpertPredict is done; 0 = off (set it to 0 when the queues hold
+   * no SpeculativeExpertPredict). */
+  int32_t speculative_prefetch_stages;
 } EkMixtralArgs;
 
 /* ABI version compiled into the library (EK_ABI_VERSION). */
