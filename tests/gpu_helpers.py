@@ -2,6 +2,9 @@
 through the megakernel (mk_llama via the C ABI) and through the CPU oracle on
 identical inputs."""
 
+import json
+import os
+
 import torch
 
 import cases
@@ -83,3 +86,14 @@ def assert_logits_within_floor(mine, ref, alt):
     rms = d.pow(2).mean().sqrt().item()
     assert rms <= rms_bound, f"rms |dlogit| {rms:.4g} > {rms_bound:.4g}"
     return d.max().item() / sd, rms / sd
+
+
+def record_parity(case: str, **values):
+    """Print a parity measurement and, when EK_PARITY_LOG names a file, append
+    it there as one JSON line (the source of the committed parity table)."""
+    line = {"case": case, **values}
+    print("parity", json.dumps(line))
+    path = os.environ.get("EK_PARITY_LOG")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(line) + "\n")
