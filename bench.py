@@ -59,6 +59,10 @@ def parse():
     ap.add_argument("--prefetch", type=int, default=0, help="L2 prefetch stages (0 = off)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-spec", action="store_true", help="Mixtral: schedule without SpeculativeExpertPredict")
+    ap.add_argument("--mixtral-tp-steps", type=int, default=64,
+                    help="with --gpus N > 1: also decode Mixtral 8x7B tensor parallel over the N GPUs")
+    ap.add_argument("--mixtral-tp-kv", type=int, default=4096)
     return ap.parse_args()
 
 
@@ -202,11 +206,17 @@ class ClockSampler:
 
 def cpu_decode_sample(name, kv, tokens):
     """Time `tokens` decode steps of the CPU oracle (a port of the reference
-    PyVM) at KV length `kv`. Returns (tokens/s, threads, seconds)."""
+    PyVM) at KV length `kv`. Returns (tokens/s, threads, seconds, note).
+
+    Mixtral (93 GB) does not fit a CPU run here: a 2-layer model of the full
+    width is timed and its per-layer cost scaled to 32 layers (the note says
+    so); the LM head is timed in full."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    if name == "mixtral":
+        return _cpu_mixtral_sample(kv, tokens)
     from megakernels.demos.latency.scheduler import LatencyScheduleBuilder
     from oracle import pyvm
 
-    torch.set_num_threads(os.cpu_count() or 1)
     model = build_model(name, kv + tokens + 1, "cpu")
     fill_kv(model, kv)
     sched = LatencyScheduleBuilder.build(model, seq_len=kv + tokens)
@@ -218,7 +228,53 @@ def cpu_decode_sample(name, kv, tokens):
         for i in range(tokens):
             _, tok = pyvm.pyvm_step(model, sched.globs, instrs, tok, kv + i)
         dt = time.perf_counter() - t0
-    return tokens / dt, torch.get_num_threads(), dt
+    note = f"{tokens} decode token(s) of the full model at KV {kv}"
+    return tokens / dt, torch.get_num_threads(), dt, note
+
+
+def _cpu_mixtral_sample(kv, tokens):
+    from megakernels.mixtral.model import MixtralConfig, MixtralForCausalLM
+    from megakernels.mixtral.scheduler import MixtralLatencyScheduleBuilder
+    from megakernels.model_types import ExtraModelConfig
+    from oracle import pyvm_mixtral
+
+    full = MixtralConfig()
+    layers = 2
+    cfg = MixtralConfig(**{**full.__dict__, "num_hidden_layers": layers})
+    model = MixtralForCausalLM.random_init(cfg, ExtraModelConfig(interleave_rope=True,
+                                                                  max_len_override=kv + tokens + 1), seed=0)
+    fill_kv(model, kv)
+    sched = MixtralLatencyScheduleBuilder.build(model, seq_len=kv + tokens)
+    g = sched.globs
+    instrs = sched.get_linear_instructions()
+    emb = model.model.embed_tokens.embed_tokens.weight
+    with torch.no_grad():
+        def step(tok, pos):
+            g.hidden_states[:] = emb[tok]
+            g.barriers.zero_()
+            g.logits.zero_()
+            g.pos_id = pos
+            pyvm_mixtral.interpret(g, instrs)
+            return int(torch.argmax(g.logits))
+
+        tok = step(0, kv - 1)  # warm-up (not timed)
+        t0 = time.perf_counter()
+        for i in range(tokens):
+            tok = step(tok, kv + i)
+        dt = time.perf_counter() - t0
+    # split the step into layers and LM head: time the LM head alone
+    lm = [ins for ins in instrs if ins.opcode() == 7]
+    with torch.no_grad():
+        t1 = time.perf_counter()
+        for ins in lm:
+            pyvm_mixtral.SOLVERS[7](g, ins)
+        lm_s = time.perf_counter() - t1
+    per_layer = (dt / tokens - lm_s) / layers
+    per_token = per_layer * full.num_hidden_layers + lm_s
+    note = (f"{tokens} decode token(s) of a {layers}-layer full-width Mixtral at KV {kv} "
+            f"({dt:.1f} s); per-layer time x {full.num_hidden_layers} layers + LM head, scaled, not measured "
+            f"on the 32-layer model (93 GB does not fit host memory)")
+    return 1.0 / per_token, torch.get_num_threads(), dt, note
 
 
 def dist_setup(n):
@@ -256,41 +312,47 @@ def barrier(world):
         dist.barrier()
 
 
+def workload_name(model, kv):
+    return f"mixtral-8x7b-kv{kv}-decode" if model == "mixtral" else f"llama-3.2-{model}-kv{kv}-decode"
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
     samples = max(1, min(args.steps, args.cpu_sample_tokens))
-    tps, cores, dt = cpu_decode_sample(args.model, args.kv, samples)
-    workload = f"llama-3.2-{args.model}-kv{args.kv}-decode"
+    tps, cores, dt, note = cpu_decode_sample(args.model, args.kv, samples)
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": samples, "warmup": 1, "ms_per_step": 1000.0 / tps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights N(0,0.02) seed 0; KV N(0,1) seed 1)",
-        "config": {"workload": workload, "kv_len": args.kv, "batch": 1},
+        "config": {"workload": workload_name(args.model, args.kv), "kv_len": args.kv, "batch": 1},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{samples} decode token(s) of the full model at KV {args.kv}, "
-                                   f"{dt:.1f} s, CPU port of the reference PyVM (reference CUDA "
+                         "sample": f"{note}, {dt:.1f} s, CPU port of the reference PyVM (reference CUDA "
                                    f"megakernel unbuildable: ThunderKittens not vendored)"},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, rank, world, local):
+def decode_leg(model_name, kv, steps, warmup, prefetch, rank, world, local, tp, with_e2e=True, spec=True):
+    """Decode `steps` tokens after `warmup` untimed ones through MK_Generator.run
+    (device-resident leg), then the same through the public API with host
+    buffers (e2e leg). Returns the timings and byte counts."""
     import mk_llama
     from megakernels.generators import MK_Generator
     from megakernels.scheduler import assign_to_sms, tensorize_instructions
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    total = args.warmup + args.steps
-    max_len = args.kv + 2 * total + 16
-    tp = args.model == "mixtral" and world > 1  # Mixtral shards; Llama runs replicas
-    model = build_model(args.model, max_len, dev, tp=(rank, world) if tp else None)
-    fill_kv(model, args.kv, rank)
-    builder, interp = builder_and_interp(args.model, args.prefetch, tp)
-    sched = builder.build(model, seq_len=args.kv + 2 * total)
+    total = warmup + steps
+    max_len = kv + 2 * total + 16
+    model = build_model(model_name, max_len, dev, tp=(rank, world) if tp else None)
+    fill_kv(model, kv, rank)
+    builder, interp = builder_and_interp(model_name, prefetch, tp)
+    if model_name == "mixtral" and not spec:
+        from megakernels.mixtral.scheduler import MixtralNoSpeculationScheduleBuilder as builder
+    sched = builder.build(model, seq_len=kv + 2 * total)
     if tp:
         from megakernels.mixtral.tp import setup_tensor_parallel
 
@@ -298,26 +360,25 @@ def run_ours(args, rank, world, local):
     tensorize_instructions(sched.globs, assign_to_sms("rr", schedule=sched))
     gen = MK_Generator(model, interp, sched)
     stream = torch.cuda.current_stream(dev)
-    g = sched.globs
-
     tok = torch.zeros(1, 1, dtype=torch.long, device=dev)
-    pos = args.kv
+    pos = kv
+    out = {}
     with torch.no_grad():
         # ---- device-resident leg: tokens stay on the GPU
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             tok = gen.run(tok, pos).view(1, 1)
             pos += 1
         torch.cuda.synchronize()
         mk_llama.check(local)
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         kv_lens = []
         barrier(world)
         torch.cuda.synchronize()
         with ClockSampler(local) as clocks:
             t_start.record(stream)
-            for i in range(args.steps):
+            for i in range(steps):
                 starts[i].record(stream)
                 tok = gen.run(tok, pos).view(1, 1)
                 ends[i].record(stream)
@@ -327,75 +388,95 @@ def run_ours(args, rank, world, local):
             torch.cuda.synchronize()
         barrier(world)
         mk_llama.check(local)
-        step_ms = t_start.elapsed_time(t_end) / args.steps
-        kernel_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        out["step_ms"] = max_over_ranks(t_start.elapsed_time(t_end) / steps, world)
+        out["kernel_ms"] = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+        out["clocks"] = clocks.summary()
+        out["alg_bytes"] = weight_bytes(model) + kv_bytes_per_token(model) * statistics.mean(kv_lens)
 
-        # ---- end-to-end leg through the public API with host buffers
-        h_in = torch.zeros(1, 1, dtype=torch.long).pin_memory()
-        h_out = torch.zeros(1, dtype=torch.long).pin_memory()
-        d_in = torch.zeros(1, 1, dtype=torch.long, device=dev)
+        if with_e2e:
+            # ---- end-to-end leg through the public API with host buffers
+            h_in = torch.zeros(1, 1, dtype=torch.long).pin_memory()
+            h_out = torch.zeros(1, dtype=torch.long).pin_memory()
+            d_in = torch.zeros(1, 1, dtype=torch.long, device=dev)
 
-        def e2e_step(p):
-            d_in.copy_(h_in, non_blocking=True)
-            h_out.copy_(gen.run(d_in, p).view(-1), non_blocking=True)
-            stream.synchronize()
-            h_in[0, 0] = h_out[0]  # the host reads the result before the next step
+            def e2e_step(p):
+                d_in.copy_(h_in, non_blocking=True)
+                h_out.copy_(gen.run(d_in, p).view(-1), non_blocking=True)
+                stream.synchronize()
+                h_in[0, 0] = h_out[0]  # the host reads the result before the next step
 
-        for _ in range(2):
-            e2e_step(pos)
-            pos += 1
-        barrier(world)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step(pos)
-            pos += 1
-        e1.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
-        mk_llama.check(local)
+            for _ in range(2):
+                e2e_step(pos)
+                pos += 1
+            barrier(world)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                e2e_step(pos)
+                pos += 1
+            e1.record(stream)
+            torch.cuda.synchronize()
+            out["e2e_ms"] = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+            mk_llama.check(local)
+    del gen, sched, model
+    torch.cuda.empty_cache()
+    return out
 
-    step_ms = max_over_ranks(step_ms, world)
-    e2e_ms = max_over_ranks(e2e_ms, world)
-    mean_kernel_ms = statistics.mean(kernel_ms)
-    alg_bytes = weight_bytes(model) + kv_bytes_per_token(model) * statistics.mean(kv_lens)
+
+def run_ours(args, rank, world, local):
+    tp = args.model == "mixtral" and world > 1  # Mixtral shards; Llama runs replicas
+    leg = decode_leg(args.model, args.kv, args.steps, args.warmup, args.prefetch, rank, world, local, tp,
+                     spec=not args.no_spec)
     peak, peak_kind = load_peaks()
-    achieved = alg_bytes / (mean_kernel_ms * 1e-3) / 1e9
+    achieved = leg["alg_bytes"] / (leg["kernel_ms"] * 1e-3) / 1e9
+
+    # the sharded path on the same GPUs: Mixtral tensor parallel over all ranks
+    mixtral_tp = None
+    if world > 1 and args.model != "mixtral" and args.mixtral_tp_steps > 0:
+        m = decode_leg("mixtral", args.mixtral_tp_kv, args.mixtral_tp_steps, 3, 0, rank, world, local, True)
+        ach = m["alg_bytes"] / (m["kernel_ms"] * 1e-3) / 1e9
+        mixtral_tp = {"workload": workload_name("mixtral", args.mixtral_tp_kv), "parallelism": f"tp{world}",
+                      "steps": args.mixtral_tp_steps, "ms_per_token": m["step_ms"],
+                      "tokens_per_s": 1000.0 / m["step_ms"], "e2e_tokens_per_s": 1000.0 / m["e2e_ms"],
+                      "ms_per_token_kernel": m["kernel_ms"],
+                      "roofline_per_gpu": {"achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                                           "algorithmic_bytes_per_launch": m["alg_bytes"]},
+                      "clocks": m["clocks"]}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.model != "mixtral":
-        del model, sched, gen
-        tps, cores, dt = cpu_decode_sample(args.model, args.kv, args.cpu_sample_tokens)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, cores, dt, note = cpu_decode_sample(args.model, args.kv, args.cpu_sample_tokens)
         cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{args.cpu_sample_tokens} decode tokens of the full model at KV {args.kv} "
-                         f"through the CPU port of the reference PyVM ({dt:.1f} s)"}
+               "sample": f"{note} through the CPU port of the reference PyVM ({dt:.1f} s)"}
     if rank != 0:
         return
-    workload = (f"mixtral-8x7b-kv{args.kv}-decode" if args.model == "mixtral"
-                else f"llama-3.2-{args.model}-kv{args.kv}-decode")
+    workload = workload_name(args.model, args.kv)
     streams = 1 if tp else world  # token streams the job decodes at once
     line = {
-        "metric": METRIC, "value": streams * 1000.0 / step_ms, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "metric": METRIC, "value": streams * 1000.0 / leg["step_ms"], "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": leg["step_ms"],
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights N(0,0.02) seed 0; KV N(0,1) seed 1)",
         "config": {"workload": workload, "kv_len": args.kv, "batch": 1,
                    "parallelism": (f"tp{world}" if tp else f"replicas{world}") if world > 1 else "single",
                    "l2_prefetch_stages": args.prefetch,
+                   "speculative_prediction": (not args.no_spec) if args.model == "mixtral" else None,
                    "l2": "no flush: the weights read per step (>= 2.5 GB) exceed the 126 MB L2"},
         "gpu_launches": args.steps,
-        "ms_per_token_kernel": mean_kernel_ms,
+        "ms_per_token_kernel": leg["kernel_ms"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "algorithmic_bytes_per_launch": leg["alg_bytes"],
                      "scope": "per GPU: this rank's shard" if tp else "per GPU",
                      "traffic": read_profile_traffic(workload)},
-        "clocks": clocks.summary(),
-        "e2e": {"value": streams * 1000.0 / e2e_ms, "unit": "tokens/s",
+        "clocks": leg["clocks"],
+        "e2e": {"value": streams * 1000.0 / leg["e2e_ms"], "unit": "tokens/s",
                 "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
         "cpu_baseline": cpu,
     }
+    if mixtral_tp is not None:
+        line["mixtral_tp"] = mixtral_tp
     print(json.dumps(line), flush=True)
 
 
