@@ -797,16 +797,16 @@ struct Consumer {
     const int R = o ? p.o_R : p.down_R;
     const int splits = o ? p.o_splits : p.down_splits;
     const int nrows = (b1 - b0) * 16;
-    // O-proj adds into the residual stream; with deferred down partials of
-    // layer l - 1 (complete before this layer's attention can finish, and in
-    // practice long before) the first row of each thread is read before the
+    // O-proj adds into the residual stream: once layer l - 1 is complete (in
+    // practice long before this layer's attention is), the first row of each
+    // thread, with layer l - 1's deferred down partials, is read before the
     // attention wait, so that its latency overlaps the wait
     const bool own_rows = o && splits == 1 && p.tp_world <= 1;
     const int nsplit = own_rows ? deferred_splits(l - 1) : 0;
     const __nv_bfloat16* xres = l == 0 ? layer0_input() : p.hidden;
     float hpre = 0.f;
     if (own_rows) {
-      if (nsplit > 0) {
+      if (l > 0) {  // the rows must hold layer l - 1's result (or its deferred partials)
         int* a = bar(l - 1, OP_DOWN - 1, 0);
         const int t = p.down_done_target;
         if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
