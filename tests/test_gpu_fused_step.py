@@ -71,10 +71,13 @@ def test_fused_argmax_takes_first_of_tied_rows(setup):
     lm = model.lm_head.lm_head.weight
     saved = lm.data.clone()
     try:
-        # rows 1234 and 77 identical and scaled up: their logits tie as the
-        # maximum, and the earlier row must win
-        lm.data[1234] = saved[3000] * 8
-        lm.data[77] = saved[3000] * 8
+        # rows 1234 and 77 set to twice the row of the (positive) largest
+        # logit: their logits tie as the new maximum, and the earlier row must win
+        l0, _, _ = unfused_step(model, sched, 5)
+        best = int(torch.argmax(l0))
+        assert l0[best] > 0
+        lm.data[1234] = saved[best] * 2
+        lm.data[77] = saved[best] * 2
         lu, _, _ = unfused_step(model, sched, 5)
         lf, _, _, tok = fused_step(model, sched, 5)
         mk_llama.check()
