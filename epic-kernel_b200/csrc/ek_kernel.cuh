@@ -305,7 +305,7 @@ struct Plan {
   int bad_word;   // >= 0: index of an out-of-range word
 };
 
-static __device__ __noinline__ Plan make_plan(const KParams& p, const Ins& ins) {
+__device__ __forceinline__ Plan make_plan(const KParams& p, const Ins& ins) {
   Plan pl;
   pl.op = ins.w[0];
   pl.layer = 0;
@@ -490,7 +490,7 @@ struct StageWalker {
 
   // `ex`: the selected (or, for prefetch, predicted) experts of a Mixtral
   // expert instruction; ignored otherwise.
-  __device__ __noinline__ void init(const KParams& p, const Ins& ins, const Plan& pl, const int* ex = nullptr) {
+  __device__ __forceinline__ void init(const KParams& p, const Ins& ins, const Plan& pl, const int* ex = nullptr) {
     op = pl.op;
     k = 0;
     ns = pl.ns;
@@ -549,7 +549,7 @@ struct StageWalker {
   // Issue the current stage (load into dst completing on bar, or an L2
   // prefetch) and advance. Returns the stage's bytes.
   template <bool PREFETCH>
-  __device__ __noinline__ uint32_t issue(const KParams& p, uint8_t* dst, uint64_t* bar) {
+  __device__ __forceinline__ uint32_t issue(const KParams& p, uint8_t* dst, uint64_t* bar) {
     uint32_t bytes;
     if (op == OP_PARTIAL) {
       const int t0 = kv_t0 + k * p.tk;
@@ -615,7 +615,7 @@ struct StageWalker {
     int copies;
     long long row_step, stage_step;
   };
-  __device__ __noinline__ int contiguous_run(const KParams& p, Run& r) {
+  __device__ __forceinline__ int contiguous_run(const KParams& p, Run& r) {
     if (op == OP_PARTIAL || chunks != 1) return 0;
     int n = groups - rg;
     if (nmat == 1) n = (int)min((long long)(ns - k), (long long)(nblocks - j) * groups - rg);
@@ -634,7 +634,7 @@ struct StageWalker {
   }
 
   // Advance over a run of n stages returned by contiguous_run.
-  __device__ __noinline__ void skip_run(const KParams& p, int n) {
+  __device__ __forceinline__ void skip_run(const KParams& p, int n) {
     k += n;
     if (nmat == 1) {
       rg += n;
