@@ -391,9 +391,9 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
 // ---------------------------------------------------------------------------
 // Allocation-free entry point.
 //
-// Some callers cannot call cudaMalloc at decode time: code running while a
-// CUDA graph is being captured, allocators that must not be re-entered,
-// embedded runtimes that reserve all device memory up front. For them the
+// Some callers cannot call cudaMalloc at decode time: allocators that must not
+// be re-entered, embedded runtimes that reserve all device memory up front and
+// hand out only their own pool. For them the
 // engine's scratch (status record, split-sum arrival counters, split partial
 // sums) lives in file-scope device arrays of fixed size that every GPU which
 // loads this library keeps until the process exits (about 0.7 MiB per GPU).

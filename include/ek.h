@@ -224,9 +224,9 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* args, void* stream);
 
 /*
  * Llama decode step that allocates nothing, for callers that cannot call
- * cudaMalloc while decoding (for example code running under CUDA graph
- * capture, or runtimes that reserve all device memory up front). This entry
- * point has no counterpart in the reference.
+ * cudaMalloc while decoding: runtimes that reserve all device memory up front
+ * and hand out only their own pool, or allocators that must not be re-entered
+ * from the decode path. This entry point has no counterpart in the reference.
  *
  * The engine's scratch lives in fixed-size device arrays inside this library
  * (about 0.7 MiB per GPU that loads it, kept until process exit): at most

@@ -1,8 +1,8 @@
 """The allocation-free entry point `ek_llama_decode_static` (include/ek.h).
 
 It exists for callers that cannot call cudaMalloc while decoding, such as
-code running under CUDA graph capture or runtimes that have reserved all
-device memory up front. It keeps the engine's scratch in fixed device arrays
+runtimes that have reserved all device memory up front or allocators that
+must not be re-entered. It keeps the engine's scratch in fixed device arrays
 inside the library instead of allocating it. This test calls it through the
 C ABI twice in a row and checks each result against the regular entry point
 (`ek_llama_decode`, via mk_llama) on identical inputs. The kernel is
@@ -72,7 +72,11 @@ def test_static_entry_matches_context_entry_twice(pos):
     expected = {n: getattr(ref.globs, n).clone() for n in OUTPUTS}
     for call in range(2):
         s = prepare(model, pos, cases.step_hidden(2048, pos))
+        torch.cuda.synchronize()
+        free_before, _ = torch.cuda.mem_get_info()
         status = _run_static(s)
+        free_after, _ = torch.cuda.mem_get_info()
+        assert free_after == free_before, f"call {call}: device memory changed by {free_before - free_after} B"
         assert int(status[0]) == 0, f"call {call}: device status {status.tolist()}"
         for n in OUTPUTS:
             assert torch.equal(getattr(s.globs, n), expected[n]), f"call {call}: {n} differs"
