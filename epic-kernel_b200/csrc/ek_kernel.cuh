@@ -63,7 +63,10 @@ constexpr int ACT_BYTES = 49152;      // activation vector + per-stage partial s
 // GEMVs split a stage's pieces over all warps), so a warp waiting on a slot is
 // never more than one lap ahead of it and any slot count works. 8 slots keep
 // the shared-memory carve-out small enough to leave L1 for the threads' stacks.
-constexpr int NUM_STAGES = 8;         // 128 KiB ring
+#ifndef EK_STAGES
+#define EK_STAGES 8
+#endif
+constexpr int NUM_STAGES = EK_STAGES;  // 8: 128 KiB ring
 constexpr int CTRL_BYTES = 1024;      // mbarriers + reduction scratch
 constexpr int SMEM_BYTES = NUM_STAGES * STAGE_BYTES + ACT_BYTES + CTRL_BYTES;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
