@@ -969,16 +969,9 @@ struct Consumer {
       for (int w = 0; w < CW; ++w) best = max(best, wbest[w]);
       atomicMax(&p.status->argmax_key, best);
       __threadfence();
-      // epoch-tagged arrival count (a count left by an earlier launch restarts)
-      const unsigned long long tag = (unsigned long long)p.epoch << 32;
-      unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(&p.status->lm_arrivals), nv;
-      while (true) {
-        nv = ((old & ~0xffffffffull) == tag) ? old + 1 : (tag | 1ull);
-        const unsigned long long prev = atomicCAS(&p.status->lm_arrivals, old, nv);
-        if (prev == old) break;
-        old = prev;
-      }
-      if ((int)(nv & 0xffffffffull) == p.lm_count) {
+      // this launch's arrival slot (cleared by block 0 of the previous launch)
+      const unsigned n = atomicAdd(&p.status->lm_arrivals[p.epoch & 3u], 1u) + 1u;
+      if ((int)n == p.lm_count) {
         __threadfence();
         const unsigned long long k = atomicMax(&p.status->argmax_key, 0ull);
         *p.out_token = (long long)(0xffffffffu - (unsigned)(k & 0xffffffffull));
@@ -1548,6 +1541,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     mbar_init(mbox_bar, 1);
     fence_mbar_init();
   }
+  if (blockIdx.x == 0 && tid == 0 && p.out_token) p.status->lm_arrivals[(p.epoch + 1u) & 3u] = 0u;
   if (tid == NC) {
     prefetch_tensormap(&p.tm_k);
     prefetch_tensormap(&p.tm_v);

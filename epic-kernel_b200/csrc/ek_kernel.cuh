@@ -122,10 +122,10 @@ struct DevStatus {
   int pad0;
   // fused argmax of the logits (Llama, output_token set): the best
   // (epoch16, ordered bf16 value, ~row) key of the launch, and the LM-head
-  // instructions finished in it (epoch << 32 | count)
+  // instructions finished per launch in a ring of 4 counters (slot epoch % 4;
+  // block 0 clears the next launch's slot when it starts)
   unsigned long long argmax_key;
-  unsigned long long lm_arrivals;
-  int pad[2];
+  unsigned lm_arrivals[4];
 };
 static_assert(sizeof(DevStatus) == 64, "status record");
 
