@@ -1541,7 +1541,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     mbar_init(mbox_bar, 1);
     fence_mbar_init();
   }
-  if (blockIdx.x == 0 && tid == 0 && p.out_token) p.status->lm_arrivals[(p.epoch + 1u) & 3u] = 0u;
+  if (blockIdx.x == 0 && tid == 0 && p.out_token) {  // the next launch's slot (the host may skip one epoch)
+    p.status->lm_arrivals[(p.epoch + 1u) & 3u] = 0u;
+    p.status->lm_arrivals[(p.epoch + 2u) & 3u] = 0u;
+  }
   if (tid == NC) {
     prefetch_tensormap(&p.tm_k);
     prefetch_tensormap(&p.tm_v);
