@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--mixtral-tp-steps", type=int, default=64,
                     help="with --gpus N > 1: also decode Mixtral 8x7B tensor parallel over the N GPUs")
     ap.add_argument("--mixtral-tp-kv", type=int, default=4096)
+    ap.add_argument("--per-opcode", action="store_true",
+                    help="Llama: HBM bandwidth of each instruction type in isolation (one JSON line each)")
+    ap.add_argument("--per-opcode-reps", type=int, default=20)
     return ap.parse_args()
 
 
@@ -480,9 +483,71 @@ def run_ours(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+OPCODE_NAMES = {1: "LayerNorm_QKV_MatVecRopeAppend", 2: "PartialAttention", 3: "AttentionReduction",
+                4: "O_ProjResidual", 5: "LayerNormDoubleMatVecSiLU", 6: "DownProjResidual", 7: "RMS_LM_Head"}
+
+
+def run_per_opcode(args, local):
+    """Achieved HBM bandwidth per instruction type (Llama): for each opcode, a
+    launch whose queues hold only that opcode's instructions of every layer
+    (dealt round-robin), with all counters preset so that no instruction waits.
+    One JSON line per opcode: bytes the instructions must read, mean launch
+    time (CUDA events), GB/s and fraction of the measured HBM peak."""
+    import mk_llama
+    from megakernels.scheduler import round_robin_assign_to_sms, tensorize_instructions
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    model = build_model(args.model, args.kv + 64, dev)
+    fill_kv(model, args.kv)
+    builder, interp = builder_and_interp(args.model, args.prefetch)
+    sched = builder.build(model, seq_len=args.kv)
+    g = sched.globs
+    linear = sched.get_linear_instructions()
+    c = model.config
+    sp = model.stacked_params
+    nb = lambda t: t.numel() * t.element_size()  # noqa: E731
+    D, kv_rows = c.head_dim, args.kv + 1
+    kv_bytes = c.num_hidden_layers * 2 * c.num_key_value_heads * D * 2 * kv_rows
+    parts = max(1, sum(1 for i in linear if i.opcode() == 2) // (c.num_hidden_layers * c.num_key_value_heads))
+    bytes_of = {1: nb(sp.qkv_proj), 2: kv_bytes, 3: c.num_hidden_layers * c.num_attention_heads * parts * (D + 1) * 4,
+                4: nb(sp.o_proj), 5: nb(sp.up_proj) + nb(sp.gate_proj), 6: nb(sp.down_proj),
+                7: nb(model.lm_head.lm_head.weight)}
+    peak, peak_kind = load_peaks()
+    reps, warm = args.per_opcode_reps, (0 if args.per_opcode_reps == 1 else 3)
+    stream = torch.cuda.current_stream(dev)
+    for op in range(1, 8):
+        instrs = [i for i in linear if i.opcode() == op]
+        if not instrs:
+            continue
+        tensorize_instructions(g, round_robin_assign_to_sms(instrs, g.sm_count()))
+        times = []
+        for it in range(warm + reps):
+            g.barriers.fill_(1 << 24)  # every wait is already satisfied
+            g.pos_id = args.kv
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            interp.interpret(g)
+            e1.record(stream)
+            if it >= warm:
+                times.append((e0, e1))
+        torch.cuda.synchronize()
+        mk_llama.check(local)
+        us = statistics.mean(a.elapsed_time(b) for a, b in times) * 1e3
+        gbs = bytes_of[op] / (us * 1e-6) / 1e9
+        print(json.dumps({"per_opcode": op, "name": OPCODE_NAMES[op], "workload": workload_name(args.model, args.kv),
+                          "instructions": len(instrs), "layers": c.num_hidden_layers, "bytes": bytes_of[op],
+                          "us_per_launch": us, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak,
+                          "peak_kind": peak_kind}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_setup(args.gpus)
+    if args.per_opcode:
+        if rank == 0:
+            run_per_opcode(args, local)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
     else:
