@@ -1,4 +1,5 @@
-"""Mixtral tensor parallel on 2 GPUs (skipped with fewer): every rank holds a
+"""Mixtral tensor parallel on 2, 4 and 8 GPUs (each case skipped when the box
+has fewer GPUs; the small config only splits in two): every rank holds a
 shard, the hidden state is all-reduced inside the megakernel over NVLink, and
 the result must match the reference interpreter's single-GPU output (router
 indices bit-exact, logits and hidden within the noise-floor bound), be
@@ -18,9 +19,6 @@ import cases
 from gpu_helpers import assert_logits_within_floor, bf16_from_bits
 
 pytestmark = pytest.mark.gpu
-
-WORLD = 2
-
 
 def _worker(rank, world, name, pos, tmp, paths):
     sys.path[:0] = paths
@@ -56,9 +54,11 @@ def _worker(rank, world, name, pos, tmp, paths):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
-@pytest.mark.parametrize("name,pos", [("small", 300), ("wide", 777)])
-def test_mixtral_tp2_matches_single_gpu_reference(golden_dir, name, pos):
+@pytest.mark.parametrize("name,pos,world", [("small", 300, 2), ("wide", 777, 2), ("wide", 777, 4), ("wide", 777, 8)])
+def test_mixtral_tp_matches_single_gpu_reference(golden_dir, name, pos, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    WORLD = world
     from oracle import pyvm, pyvm_mixtral
     from gpu_helpers import _reordered_matvec
     from megakernels.mixtral.scheduler import MixtralLatencyScheduleBuilder
