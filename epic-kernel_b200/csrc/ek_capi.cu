@@ -22,9 +22,6 @@ struct EkContext {
   size_t counters_cap = 0;  // elements
   __nv_bfloat16* partials = nullptr;
   size_t partials_cap = 0;  // elements
-  unsigned long long* ll = nullptr;  // flagged handoff words (regular entry only)
-  size_t ll_cap = 0;                 // words
-  bool ll_owned = true;              // false for the allocation-free entry's stand-in context
   unsigned epoch = 0;
   // Mixtral tensor parallelism
   int tp_world = 1, tp_rank = 0;
@@ -91,19 +88,6 @@ int encode_kv(CUtensorMap* m, const void* base, long long rows, int hkv, int d, 
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-// Flagged handoff words (zeroed: a zero word never carries a valid tag).
-int grow_ll(EkContext* ctx, size_t words) {
-  if (words <= ctx->ll_cap) return EK_SUCCESS;
-  cudaError_t e;
-  if (ctx->ll) cudaFree(ctx->ll);
-  ctx->ll = nullptr;
-  ctx->ll_cap = 0;
-  if ((e = cudaMalloc(&ctx->ll, words * 8)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(handoff words)");
-  if ((e = cudaMemset(ctx->ll, 0, words * 8)) != cudaSuccess) return cuda_fail(e, "cudaMemset(handoff words)");
-  ctx->ll_cap = words;
-  return EK_SUCCESS;
-}
 
 int grow(EkContext* ctx, size_t counters, size_t partials) {
   cudaError_t e;
@@ -179,7 +163,6 @@ void ek_context_destroy(EkContext* ctx) {
   if (ctx->status) cudaFree(ctx->status);
   if (ctx->counters) cudaFree(ctx->counters);
   if (ctx->partials) cudaFree(ctx->partials);
-  if (ctx->ll) cudaFree(ctx->ll);
   for (int r = 0; r < ctx->tp_world; ++r)
     if (ctx->tp_peer[r] && r != ctx->tp_rank) cudaIpcCloseMemHandle(ctx->tp_peer[r]);
   if (ctx->tp_buf) cudaFree(ctx->tp_buf);
@@ -373,22 +356,6 @@ int ek_llama_decode(EkContext* ctx, const EkLlamaArgs* a, void* stream) {
   p.fuse_red = (a->options & EK_OPT_FUSE_ATTENTION_REDUCTION) ? 1 : 0;
   if (p.fuse_red && p.gqa * a->max_partials > ek::MAX_GQA * 160)
     return fail(EK_E_UNSUPPORTED, "fused attention reduction: %d heads x %d partials", p.gqa, a->max_partials);
-  // flagged handoffs: column-split down projections whose partials are
-  // deferred (the residual stream then travels as flagged words), at most 64
-  // layers (the tag holds the layer in 6 bits); the allocation-free entry
-  // keeps the counter waits
-  if ((a->options & EK_OPT_FLAGGED_HANDOFF) && I / dR > 1 && H / oR == 1 && L <= 64 && ctx->ll_owned) {
-    const long long sh = H / 2, sd = (long long)(I / dR) * (H / 2), ss = I / 2, sq = (long long)Hq * D / 2;
-    const long long skv = (long long)Hkv * D, sa = sq;
-    p.ll_h = 0;
-    p.ll_d = p.ll_h + sh;
-    p.ll_s = p.ll_d + sd;
-    p.ll_q = p.ll_s + ss;
-    p.ll_kv = p.ll_q + sq;
-    p.ll_a = p.ll_kv + skv;
-    if ((rc = grow_ll(ctx, (size_t)(p.ll_a + sa)))) return rc;
-    p.ll = ctx->ll;
-  }
   p.pf_stages = a->l2_prefetch_stages > 0 ? a->l2_prefetch_stages : 0;
   p.pf_next = a->l2_prefetch_stages < 0 ? min(-a->l2_prefetch_stages, 2) : 0;
   p.pf_mlp = a->cache_flags;
@@ -488,7 +455,6 @@ extern "C" int ek_llama_decode_static(const EkLlamaArgs* a, void* stream, EkStat
       s.ready = true;
     }
     tmp.device = dev;
-    tmp.ll_owned = false;
     tmp.status = s.status;
     tmp.counters = s.counters;
     tmp.counters_cap = kStaticCounters;

@@ -265,62 +265,6 @@ struct Consumer {
     }
   }
 
-  // ---------------------------------------------------------------- flagged handoffs
-  __device__ __forceinline__ uint32_t ll_tag(int layer) const {
-    return 0x80000000u | ((p.epoch & 0x1ffffffu) << 6) | (uint32_t)(layer & 63);
-  }
-  __device__ __forceinline__ void ll_put(long long off, int w, int layer, uint32_t data) const {
-    st_relaxed_u64(p.ll + off + w, ((unsigned long long)ll_tag(layer) << 32) | data);
-  }
-  // Spin until word w carries `tag`; bounded by timeout_ns (then the failure
-  // is recorded, `bad` set, and the stale data returned).
-  __device__ __noinline__ uint32_t ll_spin(const unsigned long long* a, uint32_t tag, int opcode, int layer,
-                                           int& bad) const {
-    const uint64_t t0 = globaltimer();
-    unsigned long long v;
-    for (uint32_t it = 0;; ++it) {
-      v = ld_relaxed_u64(a);
-      if ((uint32_t)(v >> 32) == tag) break;
-      if ((it & 15u) == 15u) {
-        if (aborted(p)) { bad = 1; break; }
-        if ((long long)(globaltimer() - t0) > p.timeout_ns) {
-          record_error(p, 1, iidx, opcode, layer, (int)(v >> 32), (int)tag, -4);
-          bad = 1;
-          break;
-        }
-      }
-    }
-    return (uint32_t)v;
-  }
-  // Data of words [w0, w0 + n) of a flagged vector of `layer` (this thread's
-  // word i of k at word w0 + tid + k NC goes to out), once their tags match.
-  __device__ __forceinline__ uint32_t ll_get(long long off, int w, int layer, int opcode, int& bad) const {
-    const unsigned long long* a = p.ll + off + w;
-    const unsigned long long v = ld_relaxed_u64(a);
-    const uint32_t tag = ll_tag(layer);
-    return (uint32_t)(v >> 32) == tag ? (uint32_t)v : ll_spin(a, tag, opcode, layer, bad);
-  }
-  // Gather n words of a flagged vector into shared memory (u32 data), CTA-wide;
-  // returns whether all arrived (uniform over the consumer threads).
-  __device__ bool ll_gather(long long off, int w0, int n, int layer, int opcode, uint32_t* dst, int bad = 0) {
-#pragma unroll 1
-    for (int base = tid; base < n; base += 4 * NC) {
-      unsigned long long v[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (base + k * NC < n) v[k] = ld_relaxed_u64(p.ll + off + w0 + base + k * NC);
-      const uint32_t tag = ll_tag(layer);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int w = base + k * NC;
-        if (w >= n) continue;
-        dst[w] = (uint32_t)(v[k] >> 32) == tag ? (uint32_t)v[k]
-                                                : ll_spin(p.ll + off + w0 + w, tag, opcode, layer, bad);
-      }
-    }
-    return !named_sync_or<NC>(bad != 0);
-  }
-
   // Norm weights a thread needs (its pieces c = tid, tid + NC), loaded before
   // the counter wait so that their latency overlaps it.
   struct NormWeights {
@@ -384,30 +328,6 @@ struct Consumer {
                       pack_bf16x2(h[6], h[7]));
   }
 
-  // residual8 from flagged words: hidden after layer `lp`'s O-proj plus its
-  // nsplit deferred down partials.
-  __device__ __forceinline__ uint4 residual8_ll(int c, int lp, int nsplit, int opcode, int& bad) const {
-    uint32_t u[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) u[k] = ll_get(p.ll_h, 4 * c + k, lp, opcode, bad);
-    if (nsplit > 0) {
-      float h[8];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) { h[2 * k] = bf_lo(u[k]); h[2 * k + 1] = bf_hi(u[k]); }
-      for (int j = 0; j < nsplit; ++j) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t q = ll_get(p.ll_d + (long long)j * (p.H / 2), 4 * c + k, lp, opcode, bad);
-          h[2 * k] = bf16r(h[2 * k] + bf_lo(q));
-          h[2 * k + 1] = bf16r(h[2 * k + 1] + bf_hi(q));
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) u[k] = pack_bf16x2(h[2 * k], h[2 * k + 1]);
-    }
-    return make_uint4(u[0], u[1], u[2], u[3]);
-  }
-
   // Residual-stream value of one row: hidden plus the nsplit deferred down
   // partials, in split order.
   __device__ __forceinline__ float residual_value(const __nv_bfloat16* x, int row, int nsplit) const {
@@ -423,33 +343,17 @@ struct Consumer {
     return h;
   }
 
-  // Residual values of rows (row, row + 1), row even: from `x` plus deferred
-  // partials, or (lp >= 0) from the flagged words of layer lp.
-  __device__ __forceinline__ float2 residual_pair(const __nv_bfloat16* x, int row, int nsplit, int lp,
-                                                  int& bad) const {
-    if (lp < 0) return make_float2(residual_value(x, row, nsplit), residual_value(x, row + 1, nsplit));
-    const uint32_t u = ll_get(p.ll_h, row / 2, lp, OP_OPROJ, bad);
-    float h0 = bf_lo(u), h1 = bf_hi(u);
-    for (int j = 0; j < nsplit; ++j) {
-      const uint32_t q = ll_get(p.ll_d + (long long)j * (p.H / 2), row / 2, lp, OP_OPROJ, bad);
-      h0 = bf16r(h0 + bf_lo(q));
-      h1 = bf16r(h1 + bf_hi(q));
-    }
-    return make_float2(h0, h1);
-  }
-
   // xs[i] = bf16(w[i] * bf16(x[i] * rsqrt(mean(x^2) + eps))) for the n-vector at
   // `x` (python_vm.py:50-56), x being the residual stream with `nsplit`
   // deferred down partials added. Leaves xs in `act`.
-  __device__ bool rmsnorm_to_act(const __nv_bfloat16* x, const __nv_bfloat16* wt, int n, NormWeights nw,
-                                 int nsplit = 0, int ll_layer = -1, int opcode = 0) {
+  __device__ void rmsnorm_to_act(const __nv_bfloat16* x, const __nv_bfloat16* wt, int n, NormWeights nw,
+                                 int nsplit = 0) {
     uint4* xs4 = reinterpret_cast<uint4*>(act);
     const uint4* w4 = reinterpret_cast<const uint4*>(wt);
     float ss = 0.f;
-    int bad = 0;
 #pragma unroll 1
     for (int c = tid; c < n / 8; c += NC) {
-      uint4 v = ll_layer >= 0 ? residual8_ll(c, ll_layer, nsplit, opcode, bad) : residual8(x, c, nsplit);
+      uint4 v = residual8(x, c, nsplit);
       xs4[c] = v;
       const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -461,7 +365,7 @@ struct Consumer {
     }
     ss = warp_sum(ss);
     if (lane == 0) red[warp] = ss;
-    if (named_sync_or<NC>(bad != 0)) return false;
+    sync();
     float tot = 0.f;
 #pragma unroll
     for (int k = 0; k < CW; ++k) tot += red[k];
@@ -482,7 +386,6 @@ struct Consumer {
       xs4[c] = make_uint4(o[0], o[1], o[2], o[3]);
     }
     sync();
-    return true;
   }
 
   // Copy n bf16 (n % 8 == 0) from global to act (values other SMs wrote).
@@ -539,8 +442,7 @@ struct Consumer {
         rs = *reinterpret_cast<const float2*>(p.rope_sin + (size_t)p.pos * p.D + seg);
       }
     }
-    const bool ll = p.ll != nullptr && l > 0;  // layer l - 1's results arrive as flagged words
-    if (l > 0 && !ll) {
+    if (l > 0) {
       int* a = bar(l - 1, OP_DOWN - 1, 0);
       const int t = p.down_done_target;
       if (!wait_counters(1, &a, &t, OP_QKV, l)) { drain(pl.ns); return; }
@@ -549,11 +451,8 @@ struct Consumer {
       return;
     }
     stamp(TS_READY);
-    if (!rmsnorm_to_act(l == 0 ? layer0_input() : p.hidden, p.attn_ln + (size_t)l * p.H, p.H, nw,
-                        deferred_splits(l - 1), ll ? l - 1 : -1, OP_QKV)) {
-      drain(pl.ns);
-      return;
-    }
+    rmsnorm_to_act(l == 0 ? layer0_input() : p.hidden, p.attn_ln + (size_t)l * p.H, p.H, nw,
+                   deferred_splits(l - 1));
     stamp(TS_ACT);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
@@ -586,12 +485,7 @@ struct Consumer {
       } else {
         dst = p.v_cache + ((size_t)l * p.T + p.pos) * kdim + (row - qdim - kdim);
       }
-      const uint32_t packed = pack_bf16x2(v0, v1);
-      *reinterpret_cast<uint32_t*>(dst) = packed;
-      if (p.ll) {
-        if (row < qdim) ll_put(p.ll_q, row / 2, l, packed);
-        else ll_put(p.ll_kv, (row - qdim) / 2, l, packed);  // k rows, then v rows
-      }
+      *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(v0, v1);
     }
     sync();
     if (tid == 0) {
@@ -692,18 +586,7 @@ struct Consumer {
     using R = AttnRoles<D>;
     const int l = ins.w[1], kvh = ins.w[2], P = ins.w[3], part = ins.w[4];
     const int gqa = p.gqa, hs = kvh * gqa, bph = D / 16;
-    const bool use_ll = p.ll != nullptr;
-    // flagged path: this KV head's q rows and new k / v rows staged here
-    uint32_t* qst = reinterpret_cast<uint32_t*>(act + 24576);              // [gqa][D / 2]
-    uint32_t* kvst = reinterpret_cast<uint32_t*>(act + 24576 + MAX_GQA * D * 2);  // k [D / 2], v [D / 2]
-    if (use_ll) {
-      if (!wait_counters(0, nullptr, nullptr, OP_PARTIAL, l)) { drain(pl.ns); return; }  // abort check
-      const int hd = p.Hkv * D / 2;
-      const bool ok = ll_gather(p.ll_q, hs * D / 2, gqa * D / 2, l, OP_PARTIAL, qst) &&
-                      ll_gather(p.ll_kv, kvh * D / 2, D / 2, l, OP_PARTIAL, kvst) &&
-                      ll_gather(p.ll_kv, hd + kvh * D / 2, D / 2, l, OP_PARTIAL, kvst + D / 2);
-      if (!ok) { drain(pl.ns); return; }
-    } else {
+    {
       int* a[MAX_GQA + 2];
       int t[MAX_GQA + 2];
       for (int h = 0; h < gqa; ++h) { a[h] = bar(l, OP_QKV - 1, hs + h); t[h] = bph; }
@@ -720,16 +603,9 @@ struct Consumer {
       const int pair = lane / R::LPP, half = lane % R::LPP;
       const int stok = pair / MAX_GQA, sh = pair % MAX_GQA;
       const int rot = stok * R::LPP + half;
-      const int qh = sh < gqa ? sh : 0;
-      if (use_ll) {
-        const uint4* q4 = reinterpret_cast<const uint4*>(qst + qh * D / 2 + half * R::DPL / 2);
+      const uint4* q4 = reinterpret_cast<const uint4*>(p.q + (size_t)(hs + (sh < gqa ? sh : 0)) * D + half * R::DPL);
 #pragma unroll
-        for (int i = 0; i < R::NQ; ++i) qr[i] = q4[(i + rot) % R::NQ];
-      } else {
-        const uint4* q4 = reinterpret_cast<const uint4*>(p.q + (size_t)(hs + qh) * D + half * R::DPL);
-#pragma unroll
-        for (int i = 0; i < R::NQ; ++i) qr[i] = __ldcg(q4 + (i + rot) % R::NQ);
-      }
+      for (int i = 0; i < R::NQ; ++i) qr[i] = __ldcg(q4 + (i + rot) % R::NQ);
     }
     stamp(TS_ACT);
     float ms = -INFINITY, ls = 0.f, acc[R::VD];
@@ -746,14 +622,9 @@ struct Consumer {
     }
     // the token appended by this step's QKV instructions is read from global
     if (warp == 0 && p.pos >= tr.t_begin && p.pos < tr.t_end) {
-      if (use_ll) {
-        attend_tile<D>(reinterpret_cast<const uint8_t*>(kvst), reinterpret_cast<const uint8_t*>(kvst + D / 2), 1,
-                       false, qr, ms, ls, acc, gqa);
-      } else {
-        const size_t off = (((size_t)l * p.T + p.pos) * p.Hkv + kvh) * D;
-        attend_tile<D>(reinterpret_cast<const uint8_t*>(p.k_cache + off),
-                       reinterpret_cast<const uint8_t*>(p.v_cache + off), 1, true, qr, ms, ls, acc, gqa);
-      }
+      const size_t off = (((size_t)l * p.T + p.pos) * p.Hkv + kvh) * D;
+      attend_tile<D>(reinterpret_cast<const uint8_t*>(p.k_cache + off),
+                     reinterpret_cast<const uint8_t*>(p.v_cache + off), 1, true, qr, ms, ls, acc, gqa);
     }
     stamp(TS_STORE);
     // merge the per-warp online-softmax states
@@ -796,10 +667,6 @@ struct Consumer {
       const int head = hs + h;
       if (p.skip_red) {
         p.attn_out[(size_t)head * D + d] = __float2bfloat16_rn(out);
-        if (use_ll) {  // pairs of dims: the neighbouring lane holds d + 1
-          const float o1 = __shfl_down_sync(0xffffffffu, out, 1);
-          if ((d & 1) == 0) ll_put(p.ll_a, (head * D + d) / 2, l, pack_bf16x2(out, o1));
-        }
       } else {
         p.attn_o[((size_t)head * p.maxP + part) * D + d] = out;
         if (d == 0) p.lse[(size_t)head * p.maxP + part] = lse;
@@ -892,14 +759,10 @@ struct Consumer {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int idx = tid + k * NC;
-      if (idx >= gqa * D) continue;  // warp-uniform (gqa * D is a multiple of 64)
+      if (idx >= gqa * D) continue;
       const int h = idx / D, d = idx - h * D;
       if (terminal) {
         p.attn_out[(size_t)(hs + h) * D + d] = __float2bfloat16_rn(res[k]);
-        if (p.ll) {  // pairs of dims: the neighbouring lane holds d + 1
-          const float r1 = __shfl_down_sync(0xffffffffu, res[k], 1);
-          if ((d & 1) == 0) ll_put(p.ll_a, ((hs + h) * D + d) / 2, l, pack_bf16x2(res[k], r1));
-        }
       } else {
         const size_t row = (size_t)(hs + h) * p.maxP + out_slot;
         p.attn_o[row * D + d] = res[k];
@@ -941,32 +804,22 @@ struct Consumer {
     const bool own_rows = o && splits == 1 && p.tp_world <= 1;
     const int nsplit = own_rows ? deferred_splits(l - 1) : 0;
     const __nv_bfloat16* xres = l == 0 ? layer0_input() : p.hidden;
-    const bool use_ll = p.ll != nullptr;
-    const bool ll_in = use_ll && own_rows && l > 0;  // residual rows arrive as flagged words
-    int bad = 0;
-    float2 hpre = make_float2(0.f, 0.f);  // residual of this thread's first row pair
+    float hpre = 0.f;
     if (own_rows) {
-      if (l > 0 && !use_ll) {  // the rows must hold layer l - 1's result (or its deferred partials)
+      if (l > 0) {  // the rows must hold layer l - 1's result (or its deferred partials)
         int* a = bar(l - 1, OP_DOWN - 1, 0);
         const int t = p.down_done_target;
         if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
       }
-      if (2 * tid < nrows) hpre = residual_pair(xres, b0 * 16 + 2 * tid, nsplit, ll_in ? l - 1 : -1, bad);
+      if (tid < nrows) hpre = residual_value(xres, b0 * 16 + tid, nsplit);
     }
-    if (use_ll) {
-      if (!wait_counters(0, nullptr, nullptr, pl.op, l)) { drain(pl.ns); return; }  // abort check
-      stamp(TS_READY);
-      if (!ll_gather(o ? p.ll_a : p.ll_s, split * R / 2, R / 2, l, pl.op, reinterpret_cast<uint32_t*>(act), bad)) {
-        drain(pl.ns);
-        return;
-      }
-    } else {
+    {
       int* a = o ? bar(l, OP_REDUCTION - 1, 0) : bar(l, OP_UPGATE - 1, 0);
       const int t = o ? p.Hq : p.I / 16;
       if (!wait_counters(1, &a, &t, pl.op, l)) { drain(pl.ns); return; }
-      stamp(TS_READY);
-      copy_to_act((o ? p.attn_out : p.silu) + (size_t)split * R, R);
     }
+    stamp(TS_READY);
+    copy_to_act((o ? p.attn_out : p.silu) + (size_t)split * R, R);
     stamp(TS_ACT);
     // partial sums: [o_splits][H] for O_ProjResidual, then [down_splits][H]
     __nv_bfloat16* partials = p.split_partials + (size_t)(o ? 0 : p.o_splits) * p.H;
@@ -996,21 +849,16 @@ struct Consumer {
       if (tid == 0) red_release_add(bar(l, OP_OPROJ - 1, 0), b1 - b0);
       return;
     }
-    const bool ll_out_d = use_ll && !o && l < p.defer_down;  // deferred partials as flagged words
 #pragma unroll 1
-    for (int pi = tid; pi < nrows / 2; pi += NC) {  // row pairs
-      const int j = (2 * pi) / 16, r = (2 * pi) % 16;
-      const int row = b0 * 16 + 2 * pi;
-      const float v0 = bf16r(row_sum(part, j * spb, R, r)), v1 = bf16r(row_sum(part, j * spb, R, r + 1));
+    for (int idx = tid; idx < nrows; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      const int row = (b0 + j) * 16 + r;
+      const float v = bf16r(row_sum(part, j * spb, R, r));
       if (splits == 1) {
-        const float2 h = own_rows && pi == tid ? hpre : residual_pair(xres, row, nsplit, ll_in ? l - 1 : -1, bad);
-        const uint32_t packed = pack_bf16x2(h.x + v0, h.y + v1);
-        *reinterpret_cast<uint32_t*>(p.hidden + row) = packed;
-        if (use_ll && o) ll_put(p.ll_h, row / 2, l, packed);
-      } else if (ll_out_d) {
-        ll_put(p.ll_d + (long long)split * (p.H / 2), row / 2, l, pack_bf16x2(v0, v1));
+        const float h = own_rows && idx == tid ? hpre : residual_value(xres, row, nsplit);
+        p.hidden[row] = __float2bfloat16_rn(h + v);
       } else {
-        *reinterpret_cast<uint32_t*>(partials + (size_t)split * p.H + row) = pack_bf16x2(v0, v1);
+        partials[(size_t)split * p.H + row] = __float2bfloat16_rn(v);
       }
     }
     sync();
@@ -1049,37 +897,24 @@ struct Consumer {
   __device__ void op_upgate(const Ins& ins, const Plan& pl) {
     const int l = ins.w[1], n = ins.w[2];
     const NormWeights nw = preload_norm(p.mlp_ln + (size_t)l * p.H, p.H);
-    const bool use_ll = p.ll != nullptr;
-    if (use_ll) {
-      if (!wait_counters(0, nullptr, nullptr, OP_UPGATE, l)) { drain(pl.ns); return; }  // abort check
-    } else {
+    {
       int* a = bar(l, OP_OPROJ - 1, 0);
       const int t = p.H / 16;
       if (!wait_counters(1, &a, &t, OP_UPGATE, l)) { drain(pl.ns); return; }
     }
     stamp(TS_READY);
-    if (!rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H, nw, 0, use_ll ? l : -1, OP_UPGATE)) {
-      drain(pl.ns);
-      return;
-    }
+    rmsnorm_to_act(p.hidden, p.mlp_ln + (size_t)l * p.H, p.H, nw);
     stamp(TS_ACT);
     const int spb = stages_per_row_block(p.H);
     float* part = partials_after(p.H);
     gemv_stream(pl.ns, p.H, part);
     stamp(TS_STORE);
-    for (int pi = tid; pi < n * 8; pi += NC) {  // row pairs
-      const int j = pi / 8, r = 2 * (pi % 8);
-      float sl2[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float u = bf16r(row_sum(part, j * 2 * spb, p.H, r + e));
-        const float gt = bf16r(row_sum(part, j * 2 * spb + spb, p.H, r + e));
-        sl2[e] = bf16r(gt / (1.0f + expf(-gt))) * u;
-      }
-      const int row = ins.w[3 + j] * 16 + r;
-      const uint32_t packed = pack_bf16x2(sl2[0], sl2[1]);
-      *reinterpret_cast<uint32_t*>(p.silu + row) = packed;
-      if (use_ll) ll_put(p.ll_s, row / 2, l, packed);
+    for (int idx = tid; idx < n * 16; idx += NC) {
+      const int j = idx / 16, r = idx % 16;
+      const float u = bf16r(row_sum(part, j * 2 * spb, p.H, r));
+      const float gt = bf16r(row_sum(part, j * 2 * spb + spb, p.H, r));
+      const float sl = bf16r(gt / (1.0f + expf(-gt)));
+      p.silu[ins.w[3 + j] * 16 + r] = __float2bfloat16_rn(sl * u);
     }
     sync();
     if (tid == 0) red_release_add(bar(l, OP_UPGATE - 1, 0), n);

@@ -220,14 +220,6 @@ struct KParams {
   long long* out_token;
   int lm_count;
   int spec_stages;  // Mixtral: stages per predicted expert L2-prefetched before the router handoff
-  // Flagged handoffs (Llama; null = counter waits): producers write each pair
-  // of bf16 results as one 8-byte word {data, tag(launch, layer)}, and the
-  // consumers spin on the words themselves instead of on the counters (which
-  // are still bumped). Word offsets of the per-layer vectors: hidden after
-  // O-proj [H/2], deferred down partials [splits][H/2], SiLU [I/2], q
-  // [Hq D/2], the new k and v rows [2][Hkv D/2], attention output [Hq D/2].
-  unsigned long long* ll;
-  long long ll_h, ll_d, ll_s, ll_q, ll_kv, ll_a;
   long long timeout_ns;
   unsigned epoch;
 };

@@ -172,17 +172,6 @@ __device__ __forceinline__ void red_release_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// 8-byte relaxed (single-copy atomic) accesses for flagged handoff words.
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -193,21 +182,6 @@ __device__ __forceinline__ uint64_t globaltimer() {
 template <int NTHREADS>
 __device__ __forceinline__ void named_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NTHREADS) : "memory");
-}
-
-// Named barrier over the consumer warps that also ORs a predicate across them.
-template <int NTHREADS>
-__device__ __forceinline__ bool named_sync_or(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "n"(NTHREADS)
-      : "memory");
-  return r != 0;
 }
 
 // ---------------------------------------------------------------- bf16 helpers

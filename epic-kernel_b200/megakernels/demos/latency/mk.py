@@ -53,7 +53,6 @@ def _stream_options(globs, options):
     opts = dict(options)
     opts.setdefault("fuse_attention_reduction", getattr(globs, "attention_reduction_fusable", False))
     opts.setdefault("deferred_down_layers", getattr(globs, "deferrable_down_layers", 0))
-    opts.setdefault("flagged_handoff", getattr(globs, "flagged_handoff_ok", False))
     return opts
 
 

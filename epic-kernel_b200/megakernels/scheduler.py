@@ -234,9 +234,6 @@ def tensorize_instructions(globs: BaseGlobals, instruction_queues: list[list[Ins
 
     globs.attention_reduction_fusable = attention_reduction_fusable(globs, instruction_queues)
     globs.deferrable_down_layers = deferrable_down_layers(instruction_queues)
-    qkv_layers = [ins.layer_idx for q in instruction_queues for ins in q if ins.opcode() == 1]
-    # flagged handoffs need every layer boundary the stream crosses deferred
-    globs.flagged_handoff_ok = bool(qkv_layers) and globs.deferrable_down_layers >= max(qkv_layers)
     globs.lm_head_instructions = sum(1 for q in instruction_queues for ins in q if ins.opcode() == 7)
     globs.expert_predictions = sum(
         1 for q in instruction_queues for ins in q if type(ins).__name__ == "SpeculativeExpertPredict")

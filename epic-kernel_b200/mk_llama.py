@@ -35,9 +35,6 @@ Extra keyword-only options (defaults match the reference's behaviour):
                       column-split partials for layer l + 1 to add (the
                       interpreter passes what `tensorize_instructions` found
                       safe for the stream)
-  flagged_handoff     results travel between SMs as tagged 8-byte words that
-                      the consumers wait on (include/ek.h EK_OPT_FLAGGED_HANDOFF;
-                      the interpreter sets it when the stream allows)
   input_token, embed_weights, output_token, lm_head_instructions
                       fused token step: layer 0 reads embed_weights[input_token]
                       (int64 device scalar) instead of hidden_states, and the
@@ -72,7 +69,6 @@ EK_CACHE_WEIGHTS_EVICT_FIRST = 16
 EK_CACHE_KV_EVICT_FIRST = 32
 DEFAULT_CACHE_FLAGS = EK_CACHE_WEIGHTS_EVICT_FIRST
 EK_OPT_FUSE_ATTENTION_REDUCTION = 1
-EK_OPT_FLAGGED_HANDOFF = 2
 
 
 def _need(t: torch.Tensor, name: str, dtype, ndim: int | None = None):
@@ -91,7 +87,7 @@ def _need(t: torch.Tensor, name: str, dtype, ndim: int | None = None):
 
 def _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size,
                 cache_flags=None, prefetch_gap_ns=0, fuse_attention_reduction=False,
-                deferred_down_layers=0, flagged_handoff=False):
+                deferred_down_layers=0):
     (barriers, instructions, timings, qkv_w, attn_ln_w, o_w, mlp_ln_w, up_w, gate_w, down_w,
      lm_norm_w, lm_w, k4, v4, cos, sin, hidden, q, attn_out, lse, o_int, silu, logits) = tensors
     a = ek.EkLlamaArgs()
@@ -161,8 +157,7 @@ def _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_re
     a.timeout_ns = int(timeout_ns)
     a.cache_flags = int(DEFAULT_CACHE_FLAGS if cache_flags is None else cache_flags)
     a.prefetch_gap_ns = int(prefetch_gap_ns)
-    a.options = ((EK_OPT_FUSE_ATTENTION_REDUCTION if fuse_attention_reduction else 0)
-                 | (EK_OPT_FLAGGED_HANDOFF if flagged_handoff else 0))
+    a.options = EK_OPT_FUSE_ATTENTION_REDUCTION if fuse_attention_reduction else 0
     a.deferred_down_layers = int(deferred_down_layers)
     return a, next(iter(devices)).index
 
@@ -179,7 +174,7 @@ def mk_llama(
     *, stream=None, l2_prefetch_stages: int = 0, record_timings: bool = False,
     timeout_ns: int = 0, down_reduction_size: int = 0,
     cache_flags: int | None = None, prefetch_gap_ns: int = 0, fuse_attention_reduction: bool = False,
-    deferred_down_layers: int = 0, flagged_handoff: bool = False,
+    deferred_down_layers: int = 0,
     input_token=None, embed_weights=None, output_token=None, lm_head_instructions: int = 0,
 ):
     tensors = (barriers, instructions, timings, qkv_proj_weights, attn_ln_weights, o_proj_weights,
@@ -191,13 +186,12 @@ def mk_llama(
         cache_flags = DEFAULT_CACHE_FLAGS
     key = (tuple((t.data_ptr(), tuple(t.shape), t.dtype) if t is not None else None for t in tensors),
            l2_prefetch_stages, bool(record_timings), int(timeout_ns), down_reduction_size,
-           int(cache_flags), int(prefetch_gap_ns), bool(fuse_attention_reduction), int(deferred_down_layers),
-           bool(flagged_handoff))
+           int(cache_flags), int(prefetch_gap_ns), bool(fuse_attention_reduction), int(deferred_down_layers))
     hit = _cache.get(key)
     if hit is None:
         hit = _build_args(tensors, l2_prefetch_stages, record_timings, timeout_ns, down_reduction_size,
                           cache_flags, prefetch_gap_ns, bool(fuse_attention_reduction),
-                          int(deferred_down_layers), bool(flagged_handoff))
+                          int(deferred_down_layers))
         if len(_cache) > 64:
             _cache.clear()
         _cache[key] = hit

@@ -53,14 +53,6 @@ extern "C" {
  * schedules whose reductions are terminal over all partials in order (the
  * latency scheduler's); the counters end with the same values. */
 #define EK_OPT_FUSE_ATTENTION_REDUCTION 1
-/* Flagged handoffs between SMs: each layer's results (residual stream, SiLU,
- * q and the new k/v rows, attention output) also travel as 8-byte words that
- * carry a (launch, layer) tag, and consumers wait on those words instead of on
- * the counters (which still end with the same values). Needs column-split
- * down projections deferred over every layer boundary of the stream
- * (deferred_down_layers) and at most 64 layers; otherwise ignored. The
- * allocation-free entry ignores it. */
-#define EK_OPT_FLAGGED_HANDOFF 2
 
 typedef struct EkContext EkContext;
 
