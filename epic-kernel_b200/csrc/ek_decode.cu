@@ -57,8 +57,13 @@ __device__ __forceinline__ void stage_wait(const KParams& p, uint64_t* bar, uint
 // RPS: rows per stage. ROW_IS_J: S == 2048, so piece j of every thread lies in
 // row j of the stage at column piece tid. FULL: every stage holds 1024 pieces.
 // Only RPS == 1 splits rows into column chunks.
+#ifdef EK_GEMV_INLINE
+#define EK_GEMV_LINKAGE __forceinline__
+#else
+#define EK_GEMV_LINKAGE __noinline__
+#endif
 template <int RPS, bool ROW_IS_J, bool FULL>
-__device__ __noinline__ uint2 gemv_blocks_rps(const KParams& p, const uint8_t* stages, uint64_t* full,
+__device__ EK_GEMV_LINKAGE uint2 gemv_blocks_rps(const KParams& p, const uint8_t* stages, uint64_t* full,
                                               uint64_t* empty, uint32_t g, uint32_t broken, const uint8_t* act,
                                               int nblk, int chunks, int S, int x_base, float* part,
                                               uint32_t timing, int iidx) {
@@ -1578,10 +1583,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
   c.broken = false;
 
   Ins& ins = ins_smem[0];
+  const int* qwords = p.instructions + (size_t)blockIdx.x * p.Q * 32;
+  // instruction words one instruction ahead: warp 0's lane t holds word t of
+  // the next instruction, loaded while the current one runs
+  int next_word = (tid < 32 && p.Q > 0) ? __ldg(qwords + tid) : 0;
   for (int i = 0; i < p.Q; ++i) {
     c.iidx = i;
     // every consumer finished the previous instruction (trailing barrier)
-    if (tid < 32) ins.w[tid] = __ldg(p.instructions + ((size_t)blockIdx.x * p.Q + i) * 32 + tid);
+    if (tid < 32) {
+      ins.w[tid] = next_word;
+      if (i + 1 < p.Q) next_word = __ldg(qwords + (size_t)(i + 1) * 32 + tid);
+    }
     c.sync();
     const Plan pl = make_plan(p, ins);
     c.stamp(TS_START);
