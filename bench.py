@@ -521,6 +521,8 @@ def run_per_opcode(args, local):
         if not instrs:
             continue
         tensorize_instructions(g, round_robin_assign_to_sms(instrs, g.sm_count()))
+        if op == 6:  # as inside a full stream: split partials left for the next layer
+            g.deferrable_down_layers = c.num_hidden_layers - 1
         times = []
         for it in range(warm + reps):
             g.barriers.fill_(1 << 24)  # every wait is already satisfied
