@@ -91,6 +91,13 @@ class MK_Generator(Generator):
             return input_ids
         return torch.argmax(globs.logits, dim=-1)
 
+    def prefill(self, prompt_ids: Tensor, start_pos: int = 0) -> Tensor:
+        """Fill the KV cache with the prompt (the model's dense prefill, as
+        the reference's model forward does before MK decoding) and return the
+        first generated token (argmax of the last prompt token's logits)."""
+        logits = self.model.prefill(prompt_ids, start_pos)
+        return torch.argmax(logits, dim=-1)
+
     def generate(self, output_tokens: Tensor, prompt_len: int, ntok: int,
                  ntok_already_generated: int = 1):
         for i in range(ntok):

@@ -25,6 +25,7 @@ from dataclasses import dataclass, field
 import math
 
 import torch
+import torch.nn.functional as F
 from torch import Tensor, nn
 
 from megakernels.model_types import BatchState, ExtraModelConfig
@@ -297,6 +298,58 @@ class LlamaForCausalLM(nn.Module):
         rows = (perm.unsqueeze(0) + D * torch.arange(heads, device=self.device).unsqueeze(1)).reshape(-1)
         qkv = self.stacked_params.qkv_proj
         qkv[:, : heads * D] = qkv[:, rows]
+
+    @torch.no_grad()
+    def prefill(self, input_ids: Tensor, start_pos: int = 0) -> Tensor:
+        """Run n prompt tokens (positions start_pos .. start_pos + n - 1) through
+        the model as dense matrix products with causal attention, append their
+        K/V rows to the cache, and return the last token's logits. This is the
+        reference's prefill branch (megakernels/llama.py:90-133 of epic-kernel:
+        K/V written at the positions, then scaled-dot-product attention with a
+        causal mask); the decode megakernel then continues at start_pos + n.
+        Rounding follows the decode path: bf16 activations between ops, fp32
+        accumulation inside each product, RMSNorm as the interpreter's."""
+        c, sp = self.config, self.stacked_params
+        k_cache, v_cache = self.stacked_kv_cache
+        ids = input_ids.reshape(-1).to(self.device)
+        n, D = ids.numel(), c.head_dim
+        Hq, Hkv = c.num_attention_heads, c.num_key_value_heads
+        end = start_pos + n
+        assert n >= 1 and end <= self.max_len(), "prompt beyond the KV cache"
+        pos = torch.arange(start_pos, end, device=self.device)
+        cos, sin = self.model.rope_cos[pos].unsqueeze(1), self.model.rope_sin[pos].unsqueeze(1)  # [n, 1, D]
+
+        def norm(x, w):
+            xf = x.float()
+            return w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + c.rms_norm_eps)).to(x.dtype)
+
+        def rope(x):  # [n, heads, D] bf16 -> fp32 rotary -> bf16
+            if self.extra_config.interleave_rope:
+                rot = torch.stack((-x[..., 1::2], x[..., 0::2]), dim=-1).reshape(x.shape)
+            else:
+                rot = torch.cat((-x[..., D // 2 :], x[..., : D // 2]), dim=-1)
+            return (x * cos + rot * sin).to(x.dtype)
+
+        # causal mask with the cached prefix: query i sees keys 0 .. start_pos + i
+        mask = torch.arange(end, device=self.device).unsqueeze(0) <= pos.unsqueeze(1)  # [n, end]
+        h = self.model.embed_tokens.embed_tokens.weight[ids]  # [n, H]
+        for l in range(c.num_hidden_layers):
+            qkv = norm(h, sp.attn_ln_weight[l]) @ sp.qkv_proj[l].T
+            q = rope(qkv[:, : Hq * D].view(n, Hq, D))
+            k = rope(qkv[:, Hq * D : (Hq + Hkv) * D].view(n, Hkv, D))
+            v = qkv[:, (Hq + Hkv) * D :].view(n, Hkv, D)
+            k_cache[l, 0, start_pos:end] = k
+            v_cache[l, 0, start_pos:end] = v
+            keys = k_cache[l, 0, :end].transpose(0, 1).unsqueeze(0)  # [1, Hkv, end, D]
+            vals = v_cache[l, 0, :end].transpose(0, 1).unsqueeze(0)
+            o = F.scaled_dot_product_attention(q.transpose(0, 1).unsqueeze(0), keys, vals, attn_mask=mask,
+                                               scale=1.0 / math.sqrt(D), enable_gqa=True)
+            h = h + o[0].transpose(0, 1).reshape(n, Hq * D) @ sp.o_proj[l].T
+            x = norm(h, sp.mlp_ln_weight[l])
+            up, gate = x @ sp.up_proj[l].T, x @ sp.gate_proj[l].T
+            h = h + (F.silu(gate) * up) @ sp.down_proj[l].T
+        self.prefill_hidden = h[-1].clone()
+        return self.lm_head.lm_head(self.lm_head.input_norm(h[-1]))
 
     def setup_caches(self):
         shape = (
