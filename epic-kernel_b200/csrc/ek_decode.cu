@@ -996,10 +996,12 @@ struct Consumer {
   // counter per 16-row block), then wait until all ranks pushed them here.
   // Call after a consumer barrier that follows the pushes.
   __device__ bool tp_exchange(long long cnt_off, int l, int b0, int b1, int opcode) {
-    if (tid == 0) {
-      __threadfence_system();
-      for (int r = 0; r < p.tp_world; ++r)
-        for (int b = b0; b < b1; ++b) red_release_sys_add(tp_counter(r, cnt_off, l * (p.H / 16) + b), 1);
+    // one system-scope release per (rank, block), issued in parallel by the
+    // lanes of warp 0 (serially they cost one NVLink round trip each)
+    if (warp == 0) {
+      const int nb = b1 - b0;
+      for (int k = lane; k < p.tp_world * nb; k += 32)
+        red_release_sys_add(tp_counter(k / nb, cnt_off, l * (p.H / 16) + b0 + k % nb), 1);
     }
     bool ok = true;
     const int target = p.tp_world * (int)p.tp_step;
@@ -1208,10 +1210,7 @@ struct Consumer {
           atomicAdd(reinterpret_cast<__nv_bfloat16*>(p.tp_peer[rk] + p.tp_off_logits) + row, v);
       }
       sync();
-      if (tid == 0) {
-        __threadfence_system();
-        for (int rk = 0; rk < p.tp_world; ++rk) red_release_sys_add(tp_counter(rk, p.tp_off_cnt_lm, 0), 1);
-      }
+      if (warp == 0 && lane < p.tp_world) red_release_sys_add(tp_counter(lane, p.tp_off_cnt_lm, 0), 1);
       return;
     }
     for (int idx = tid; idx < (b1 - b0) * 16; idx += NC) {
