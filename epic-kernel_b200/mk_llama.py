@@ -217,6 +217,49 @@ def mk_llama(
     )
 
 
+class PreparedStep:
+    """The fused token step's launch with everything but the per-step values
+    prepared once: build it from the same positional tensors and options as
+    `mk_llama`, then `launch(pos_id, input_token, output_token)` per token.
+    Per call it only writes those three fields and calls `ek_llama_decode`
+    (no tensor checks or cache lookups); the tensors given at construction must
+    stay allocated and in place."""
+
+    def __init__(self, *tensors_and_scalars, embed_weights, lm_head_instructions, stream=None, **options):
+        tensors = tensors_and_scalars[:23]
+        pos_id, attn_scale, rms_norm_eps, skip_attn_reduction = tensors_and_scalars[23:27]
+        opts = dict(options)
+        cache_flags = opts.pop("cache_flags", None)
+        self.args, self.device = _build_args(
+            tensors, opts.pop("l2_prefetch_stages", 0), opts.pop("record_timings", False),
+            opts.pop("timeout_ns", 0), opts.pop("down_reduction_size", 0),
+            DEFAULT_CACHE_FLAGS if cache_flags is None else cache_flags, opts.pop("prefetch_gap_ns", 0),
+            bool(opts.pop("fuse_attention_reduction", False)), int(opts.pop("deferred_down_layers", 0)))
+        if opts:
+            raise ValueError(f"PreparedStep: unknown options {sorted(opts)}")
+        a = self.args
+        a.attn_scale = float(attn_scale)
+        a.rms_norm_eps = float(rms_norm_eps)
+        a.skip_attn_reduction = int(bool(skip_attn_reduction))
+        a.embed_weights = _need(embed_weights, "embed_weights", _BF16, 2)
+        a.lm_head_instructions = int(lm_head_instructions)
+        self.ctx = ek.context_for(self.device)
+        self.fn = ek.load_library().ek_llama_decode
+        self.args_ref = ctypes.byref(a)
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        self.stream = ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+    def launch(self, pos_id: int, input_token: torch.Tensor, output_token: torch.Tensor):
+        if not (input_token.is_cuda and output_token.is_cuda):
+            raise ValueError("PreparedStep.launch: token tensors must be CUDA tensors")
+        a = self.args
+        a.pos_id = pos_id
+        a.input_token = input_token.data_ptr()
+        a.output_token = output_token.data_ptr()
+        ek.check(self.fn(self.ctx.handle, self.args_ref, self.stream), "ek_llama_decode")
+
+
 def check(device: int | None = None, clear: bool = True):
     """Synchronise and raise `EngineError` if a launch recorded a device failure."""
     if device is None:
