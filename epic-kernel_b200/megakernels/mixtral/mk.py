@@ -64,7 +64,7 @@ class MixtralMK_Interpreter(MK_Interpreter):
 
 
 # ring stages per predicted expert prefetched into L2 before the router's choice
-SPECULATIVE_PREFETCH_STAGES = 16
+SPECULATIVE_PREFETCH_STAGES = 8
 
 
 def stream_options(globs, options):
