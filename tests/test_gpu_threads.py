@@ -66,12 +66,12 @@ def test_two_threads_two_contexts_one_gpu():
         # serial reference results
         expected = []
         for (s, init), ctx, st in zip(cases_, ctxs, streams):
-            _reset(s, init)
-            torch.cuda.synchronize()
-            a = _args(s)
-            assert lib.ek_llama_decode(ctx, ctypes.byref(a), ctypes.c_void_p(st.cuda_stream)) == 0
-            torch.cuda.synchronize()
-            expected.append({n: getattr(s.globs, n).clone() for n in OUTPUTS})
+            with torch.cuda.stream(st):
+                _reset(s, init)
+                a = _args(s)
+                assert lib.ek_llama_decode(ctx, ctypes.byref(a), ctypes.c_void_p(st.cuda_stream)) == 0
+                expected.append({n: getattr(s.globs, n).clone() for n in OUTPUTS})
+            st.synchronize()
         # concurrent: each thread launches ROUNDS steps on its own context and stream
         errors = []
         results = [[], []]
@@ -80,14 +80,14 @@ def test_two_threads_two_contexts_one_gpu():
             try:
                 s, init = cases_[k]
                 a = _args(s)
-                for _ in range(ROUNDS):
-                    with torch.cuda.stream(streams[k]):
+                with torch.cuda.stream(streams[k]):  # resets, launches and copies in stream order
+                    for _ in range(ROUNDS):
                         _reset(s, init)
-                    rc = lib.ek_llama_decode(ctxs[k], ctypes.byref(a), ctypes.c_void_p(streams[k].cuda_stream))
-                    if rc:
-                        errors.append(lib.ek_last_error())
+                        rc = lib.ek_llama_decode(ctxs[k], ctypes.byref(a), ctypes.c_void_p(streams[k].cuda_stream))
+                        if rc:
+                            errors.append(lib.ek_last_error())
+                        results[k].append({n: getattr(s.globs, n).clone() for n in OUTPUTS})
                     streams[k].synchronize()
-                    results[k].append({n: getattr(s.globs, n).clone() for n in OUTPUTS})
             except Exception as e:  # noqa: BLE001
                 errors.append(repr(e))
 
