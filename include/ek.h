@@ -8,6 +8,11 @@
  * context's scratch has grown to the model's size (the first call on a
  * context allocates it).
  *
+ * Threads: calls on different contexts may come from different host threads
+ * at the same time (each call stages its kernel parameters on its own stack;
+ * the device-wide set-up is per device and guarded). One context serves one
+ * decode step at a time.
+ *
  * Errors: a nonzero return is a host-side rejection (bad argument, CUDA launch
  * failure); ek_last_error() describes it. Device-side failures (a cross-SM wait
  * that timed out, a malformed instruction) do not stop the host. The kernel
