@@ -64,7 +64,7 @@ def parse():
                     help="with --gpus N > 1: also decode Mixtral 8x7B tensor parallel over the N GPUs")
     ap.add_argument("--mixtral-tp-kv", type=int, default=4096)
     ap.add_argument("--per-opcode", action="store_true",
-                    help="Llama: HBM bandwidth of each instruction type in isolation (one JSON line each)")
+                    help="HBM bandwidth of each instruction type in isolation (one JSON line each)")
     ap.add_argument("--per-opcode-reps", type=int, default=20)
     return ap.parse_args()
 
@@ -488,7 +488,7 @@ OPCODE_NAMES = {1: "LayerNorm_QKV_MatVecRopeAppend", 2: "PartialAttention", 3: "
 
 
 def run_per_opcode(args, local):
-    """Achieved HBM bandwidth per instruction type (Llama): for each opcode, a
+    """Achieved HBM bandwidth per instruction type (Llama or Mixtral): for each opcode, a
     launch whose queues hold only that opcode's instructions of every layer
     (dealt round-robin), with all counters preset so that no instruction waits.
     One JSON line per opcode: bytes the instructions must read, mean launch
@@ -511,17 +511,27 @@ def run_per_opcode(args, local):
     kv_bytes = c.num_hidden_layers * 2 * c.num_key_value_heads * D * 2 * kv_rows
     parts = max(1, sum(1 for i in linear if i.opcode() == 2) // (c.num_hidden_layers * c.num_key_value_heads))
     bytes_of = {1: nb(sp.qkv_proj), 2: kv_bytes, 3: c.num_hidden_layers * c.num_attention_heads * parts * (D + 1) * 4,
-                4: nb(sp.o_proj), 5: nb(sp.up_proj) + nb(sp.gate_proj), 6: nb(sp.down_proj),
-                7: nb(model.lm_head.lm_head.weight)}
+                4: nb(sp.o_proj), 7: nb(model.lm_head.lm_head.weight)}
+    names = dict(OPCODE_NAMES)
+    if args.model == "mixtral":  # the k selected experts of each layer, plus the router
+        k, E = c.num_experts_per_tok, c.num_local_experts
+        bytes_of[5] = (nb(sp.expert_gate) + nb(sp.expert_up)) * k // E + nb(sp.router_weight)
+        bytes_of[6] = nb(sp.expert_down) * k // E
+        bytes_of[8] = nb(sp.router_weight)
+        names.update({5: "RmsRouterUpgate", 6: "ExpertDownProjFused", 7: "Mixtral_RMS_LM_Head",
+                      8: "SpeculativeExpertPredict"})
+    else:
+        bytes_of[5] = nb(sp.up_proj) + nb(sp.gate_proj)
+        bytes_of[6] = nb(sp.down_proj)
     peak, peak_kind = load_peaks()
     reps, warm = args.per_opcode_reps, (0 if args.per_opcode_reps == 1 else 3)
     stream = torch.cuda.current_stream(dev)
-    for op in range(1, 8):
+    for op in range(1, 9):
         instrs = [i for i in linear if i.opcode() == op]
         if not instrs:
             continue
         tensorize_instructions(g, round_robin_assign_to_sms(instrs, g.sm_count()))
-        if op == 6:  # as inside a full stream: split partials left for the next layer
+        if op == 6 and args.model != "mixtral":  # as inside a full stream: partials left for the next layer
             g.deferrable_down_layers = c.num_hidden_layers - 1
         times = []
         for it in range(warm + reps):
@@ -537,7 +547,7 @@ def run_per_opcode(args, local):
         mk_llama.check(local)
         us = statistics.mean(a.elapsed_time(b) for a, b in times) * 1e3
         gbs = bytes_of[op] / (us * 1e-6) / 1e9
-        print(json.dumps({"per_opcode": op, "name": OPCODE_NAMES[op], "workload": workload_name(args.model, args.kv),
+        print(json.dumps({"per_opcode": op, "name": names[op], "workload": workload_name(args.model, args.kv),
                           "instructions": len(instrs), "layers": c.num_hidden_layers, "bytes": bytes_of[op],
                           "us_per_launch": us, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak,
                           "peak_kind": peak_kind}), flush=True)
