@@ -1301,7 +1301,14 @@ __device__ void prefetch_instruction(const KParams& p, int q, int i, Ins* ins) {
     StageWalker::Run r;
     const int n = w.contiguous_run(p, r);
     if (n > 0) {
-      if (r.copies == 1 && r.stage_step == (long long)r.bytes) {
+      if (r.chunks > 1) {  // contiguous whole rows in chunks of two sizes
+        const uint8_t* src = r.src;
+        for (int t = 0; t < n; ++t) {
+          const uint32_t sb = (r.c0 + t) % r.chunks == r.chunks - 1 ? r.last_bytes : r.bytes;
+          bulk_prefetch_l2(src, sb);
+          src += sb;
+        }
+      } else if (r.copies == 1 && r.stage_step == (long long)r.bytes) {
         bulk_prefetch_l2(r.src, r.bytes * (uint32_t)n);
       } else {
         for (int t = 0; t < n; ++t)
@@ -1475,12 +1482,13 @@ __device__ void run_loader(const KParams& p, Ring ring, const int* mbox, uint64_
             p.timings[((size_t)q * p.Q + i) * 128 + TS_STAGE_LOAD + wk.k + t] = (int)(globaltimer() & 0x7fffffff);
           uint64_t* fb = &ring.full[ring.slot];
           uint8_t* dst = ring.stages + (size_t)ring.slot * STAGE_BYTES;
-          mbar_arrive_expect_tx(fb, rr.bytes * (uint32_t)rr.copies);
+          const uint32_t sb = (rr.chunks > 1 && (rr.c0 + t) % rr.chunks == rr.chunks - 1) ? rr.last_bytes : rr.bytes;
+          mbar_arrive_expect_tx(fb, sb * (uint32_t)rr.copies);
           if (ring_ef)
-            for (int c = 0; c < rr.copies; ++c) bulk_load_hint(dst + c * rr.bytes, rr.src + c * rr.row_step, rr.bytes, fb, pol_ef);
+            for (int c = 0; c < rr.copies; ++c) bulk_load_hint(dst + c * sb, rr.src + c * rr.row_step, sb, fb, pol_ef);
           else
-            for (int c = 0; c < rr.copies; ++c) bulk_load(dst + c * rr.bytes, rr.src + c * rr.row_step, rr.bytes, fb);
-          rr.src += rr.stage_step;
+            for (int c = 0; c < rr.copies; ++c) bulk_load(dst + c * sb, rr.src + c * rr.row_step, sb, fb);
+          rr.src += rr.chunks > 1 ? (long long)sb : rr.stage_step;
           ring_advance(ring);
           ++g_load;
         }

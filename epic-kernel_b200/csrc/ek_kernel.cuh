@@ -612,14 +612,36 @@ struct StageWalker {
   // further (one copy per stage for whole rows, one per row for row segments
   // of a column split). 0 if the current stage needs the general path. The
   // run's bounds and alignment are checked here, once.
+  // A run of whole rows longer than a stage (chunks > 1; Mixtral's expert
+  // down projection, 14336 columns) is contiguous too: its stages alternate
+  // between full chunks of `bytes` and a last chunk of `last_bytes`, and the
+  // source advances by each stage's size (chunk c0 first).
   struct Run {
     const uint8_t* src;
-    uint32_t bytes;
-    int copies;
+    uint32_t bytes, last_bytes;
+    int copies, chunks, c0;
     long long row_step, stage_step;
   };
   __device__ __forceinline__ int contiguous_run(const KParams& p, Run& r) {
-    if (op == OP_PARTIAL || chunks != 1) return 0;
+    if (op == OP_PARTIAL) return 0;
+    r.chunks = chunks;
+    r.c0 = c;
+    if (chunks != 1) {
+      if (S != stride || col0 != 0 || rps != 1 || nmat != 1) return 0;
+      const long long per_expert = (long long)(nblocks < (1 << 29) ? nblocks : 0) * groups * chunks;
+      const long long at = ((long long)j * groups + rg) * chunks + c;
+      const int n = (int)min((long long)(ns - k), per_expert - at);
+      const long long row = row_base + rg;
+      r.copies = 1;
+      r.bytes = STAGE_BYTES;
+      r.last_bytes = (uint32_t)(S - (chunks - 1) * (STAGE_BYTES / 2)) * 2;
+      r.row_step = r.stage_step = 0;
+      r.src = reinterpret_cast<const uint8_t*>(mat[m] + row * stride + (long long)c * (STAGE_BYTES / 2));
+      if (n < 1 || row < 0 || row + (c + n + chunks - 1) / chunks > mat_rows || r.last_bytes == 0 ||
+          r.last_bytes > (uint32_t)STAGE_BYTES || ((reinterpret_cast<uintptr_t>(r.src) | r.last_bytes) & 15u))
+        return 0;
+      return n;
+    }
     int n = groups - rg;
     if (nmat == 1) n = (int)min((long long)(ns - k), (long long)(nblocks - j) * groups - rg);
     const long long row = row_base + (long long)rg * rps;
@@ -638,6 +660,20 @@ struct StageWalker {
 
   // Advance over a run of n stages returned by contiguous_run.
   __device__ __forceinline__ void skip_run(const KParams& p, int n) {
+    if (chunks != 1) {  // whole rows in chunks, one matrix, within one expert's blocks
+      const long long at = ((long long)j * groups + rg) * chunks + c + n;
+      k += n;
+      j = (int)(at / (groups * chunks));
+      const int rem = (int)(at % (groups * chunks));
+      rg = rem / chunks;
+      c = rem % chunks;
+      if (j == nblocks) {
+        j = 0;
+        ++es;
+      }
+      if (k < ns) row_base = block_row(p, j);
+      return;
+    }
     k += n;
     if (nmat == 1) {
       rg += n;
