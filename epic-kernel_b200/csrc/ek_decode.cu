@@ -248,11 +248,7 @@ struct Consumer {
           __nanosleep(32);
         }
       }
-      // the abort word is read here only for a pure check (n == 0); a wait
-      // that spun has checked it in its loop, and one already satisfied may
-      // proceed (its inputs exist; the launch still ends through the waits
-      // that other failures leave unsatisfied)
-      if (ok && n == 0 && aborted(p)) ok = 0;
+      if (ok && aborted(p)) ok = 0;
       *flag = ok;
     }
     sync();
