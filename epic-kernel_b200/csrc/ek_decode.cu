@@ -98,10 +98,18 @@ __device__ EK_GEMV_LINKAGE uint2 gemv_blocks_rps(const KParams& p, const uint8_t
         const int x0 = c * (STAGE_BYTES / 2);
         const int npieces = FULL ? 1024 : RPS * (min(STAGE_BYTES / 2, S - x0) / 8);
         const uint4* xc = xs4 + x0 / 8;
+        // explicit shared-memory loads (the pointers arrive as generic
+        // addresses); the activation piece is shared by the 4 rows of a stage
+        // when ROW_IS_J
+        const uint32_t wbase = smem_u32(w4), xbase = smem_u32(xc);
+        uint4 xrow = make_uint4(0, 0, 0, 0);
+        if (ROW_IS_J) xrow = lds128(xbase + pc[0] * 16);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (!FULL && tid + 256 * j >= npieces) continue;  // warp-uniform
-          const float d = dot8_bf16(w4[tid + 256 * j], xc[pc[j]], 0.f);
+          const uint4 wv = lds128(wbase + (tid + 256 * j) * 16);
+          const uint4 xv = ROW_IS_J ? xrow : lds128(xbase + pc[j] * 16);
+          const float d = dot8_bf16(wv, xv, 0.f);
           if (RPS == 1) {
             acc[rg] += d;
           } else if (ROW_IS_J) {

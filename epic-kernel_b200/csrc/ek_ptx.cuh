@@ -184,6 +184,13 @@ __device__ __forceinline__ void named_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NTHREADS) : "memory");
 }
 
+// 16-byte shared-memory load at a shared-window address.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
 // ---------------------------------------------------------------- bf16 helpers
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
